@@ -1,0 +1,339 @@
+"""Benchmark: sparse training step of a Qwen3-30B-A3B-shaped MoE layer.
+
+One step = router + dispatch + grouped int4 SwiGLU GEMMs + combine (forward),
+the full backward (combine, router, both dX GEMMs, dX gather), expert-weight
+gradients at the 0.5% selected coordinates, and the SparseAdam updates of the
+expert masters (with the overlay write-back) and of the full router.
+Workload: T=4096 tokens, H=2048, E=128 experts, top-8,
+I=768, bf16 activations, int4 group-128 experts; synthetic seeded data.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N>1 runs under torchrun: each rank owns its own tokens and a full replica of
+the layer (weak scaling); value = all ranks' tokens / max-over-ranks time.
+``--impl reference`` times the CPU restatement of the reference's own path
+(the dense-masked expert loop, usaf/qwen3moe_dml.py:24-86, with capture and
+SparseAdam) on the host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(T=4096, H=2048, E=128, k=8, I=768, frac=0.005, lr=1e-4)
+METRIC = "training tokens/s per step (Qwen3-30B-A3B-shape, int4, 0.5% sparse)"
+UNIT = "tokens/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu),
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        try:
+            rows = [r.split(",") for r in open(self.path).read().strip().splitlines()]
+            sm = [float(r[0]) for r in rows if r and r[0].strip().replace(".", "").isdigit()]
+            mx = float(rows[0][1]) if rows else None
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            reasons = sorted({names[i] for r in rows for i in range(4)
+                              if len(r) > 2 + i and "Active" in r[2 + i] and "Not" not in r[2 + i]})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                    "reasons": reasons, "samples": len(sm)}
+        except Exception as e:  # noqa: BLE001
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": str(e)[:80]}
+
+
+# ------------------------------------------------------------------ ours ---
+def build_layer(dev, seed: int):
+    from usaf_b200.engine import Projection
+    from usaf_b200.layer import SparseMoELayer
+    from usaf_b200.quantization import quantize_4bit
+    T, H, E, k, I = CFG["T"], CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    w_r = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    projs = {}
+    for n, shape in (("gate_up_proj", (E, 2 * I, H)), ("down_proj", (E, H, I))):
+        w = torch.randn(*shape, device=dev, generator=g) * 0.02
+        q, s, z, _ = quantize_4bit(w, 128)
+        del w
+        projs[n] = Projection(q, s, z, shape, 128, torch.bfloat16)
+    dy = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    layer = SparseMoELayer(w_r, projs["gate_up_proj"], projs["down_proj"], k, T)
+    store = layer.importance(x, dy, CFG["frac"])
+    layer.init_selection(store.select(CFG["frac"]), lr=CFG["lr"])
+    torch.cuda.synchronize()
+    return layer, x, dy
+
+
+def run_ours(args, rank, world, local_rank):
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    import usaf_b200  # noqa: F401
+    from usaf_b200 import _lib
+    layer, x, dy = build_layer(dev, 1 + rank)
+    T = CFG["T"]
+    blk = layer.block
+    # timed kernel: the grouped gate_up dequant GEMM (+SwiGLU) of the forward
+    k_ev = []
+    orig_call = _lib.call
+
+    def step(xs, dys):
+        return layer.train_step(xs, dys)
+
+    for _ in range(args.warmup):
+        step(x, dy)
+    torch.cuda.synchronize()
+    blk.check()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+    def timed_call(name, *a):
+        if name == "usaf_expert_gate_up_fwd":
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            orig_call(name, *a)
+            e1.record()
+            k_ev.append((e0, e1))
+        else:
+            orig_call(name, *a)
+
+    import usaf_b200.engine as eng
+    eng.call = timed_call
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        start.record()
+        for _ in range(args.steps):
+            step(x, dy)
+        end.record()
+        torch.cuda.synchronize()
+    eng.call = orig_call
+    blk.check()
+    ms = start.elapsed_time(end) / args.steps
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
+    n_pairs = blk.n_pairs_host()
+
+    # end-to-end through the public API with host buffers
+    xh = x.cpu().pin_memory()
+    dyh = dy.cpu().pin_memory()
+    loss = torch.empty(1, device=dev)
+    lossh = torch.empty(1).pin_memory()
+    xd = torch.empty_like(x)
+    dyd = torch.empty_like(dy)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        dyd.copy_(dyh, non_blocking=True)
+        y, _, _ = layer.train_step(xd, dyd)
+        _lib.call("usaf_dot", _lib.ptr(y), _lib.ptr(dyd), _lib.BF16, y.numel(), _lib.ptr(loss),
+                  _lib.stream())
+        lossh.copy_(loss, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return float(lossh.item())
+
+    for _ in range(2):
+        e2e_step()
+    if world > 1:
+        torch.distributed.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, kern_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms, kern_ms = t.tolist()
+
+    hbm, tflops, src = peaks()
+    H, I = CFG["H"], CFG["I"]
+    flops = 2.0 * n_pairs * (2 * I) * H
+    achieved = flops / (kern_ms * 1e-3) / 1e12
+    launches = count_launches()
+    out = {
+        "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights quantized to int4 g128)",
+        "config": {"workload": "C2: one Qwen3-30B-A3B MoE layer, fwd+bwd+sparse grads+SparseAdam",
+                   "T": T, "H": H, "E": CFG["E"], "top_k": CFG["k"], "I": I, "active_frac": CFG["frac"],
+                   "routed_pairs": n_pairs, "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "working set (~1.5 GB int4 weights + activations) exceeds the 126 MB L2"},
+        "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
+                "h2d_bytes_per_step": x.numel() * 2 + dy.numel() * 2, "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "tensor", "kernel": "usaf_expert_gate_up_fwd (grouped int4 GEMM + SwiGLU)",
+                     "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
+                     "frac": achieved / tflops, "peak_source": src, "kernel_ms": kern_ms,
+                     "traffic": None},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+    }
+    return out
+
+
+def count_launches():
+    """Kernel launches of one train_step (counted from the C-ABI call sequence)."""
+    # router fwd 2, dispatch 4, gate_up 2, down 1, combine 1, combine_bwd 1,
+    # router bwd 3, down bwd 2, gate_up bwd 1, gather_dx 1, sddmm 2, adam 2 (+1 router)
+    return 23
+
+
+# ------------------------------------------------------------- reference ---
+def run_reference_cpu(sample_tokens: int, iters: int):
+    """Time the oracle restatement of the reference's CPU path: dense-masked
+    expert loop (every expert on every token) with SparseGradStore capture,
+    then SparseAdam over the masters and the router."""
+    import numpy as np
+    from oracle import moe as omoe
+    from oracle import quant as oquant
+    torch.set_num_threads(os.cpu_count())
+    T, H, E, k, I = sample_tokens, CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    torch.manual_seed(1)
+    x = torch.randn(T, H).to(torch.bfloat16)
+    w_r = (torch.randn(E, H) * 0.02).to(torch.bfloat16)
+    dense, active, shapes = [], {}, {}
+    gen = np.random.default_rng(0)
+    for n, shape in (("gate_up_proj", (E, 2 * I, H)), ("down_proj", (E, H, I))):
+        w = (torch.randn(*shape) * 0.02).numpy()
+        q, s, z, _ = oquant.quantize_4bit(w, 128)
+        del w
+        d = oquant.dequantize_4bit(q, s, z, shape, 128)
+        dense.append(torch.from_numpy(d).to(torch.bfloat16))
+        numel = int(np.prod(shape))
+        name = f"layer.mlp.experts.{n}"
+        active[name] = torch.from_numpy(gen.choice(numel, int(numel * CFG["frac"]), replace=False))
+        shapes[name] = shape
+    dy = torch.randn(T, H).to(torch.bfloat16)
+    masters = {n: dense[i].float().reshape(-1)[active[n]].clone()
+               for i, n in enumerate(shapes)}
+    times = []
+    for it in range(iters + 1):
+        t0 = time.perf_counter()
+        store = omoe.SparseGradStore(active, shapes)
+        res = omoe.block_step(x, w_r, dense[0], dense[1], dy, k, True, capture=store.add,
+                              prefix="layer.mlp.experts", experts="dense")
+        opt = omoe.SparseAdam({n: masters[n] for n in shapes}, active, compact_params=True)
+        opt.step(store.compact)
+        ropt = omoe.SparseAdam({"r": w_r.clone()}, {"r": torch.arange(E * H)})
+        ropt.step({"r": res["dW_r"]})
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times[1:])
+    return T / med, med
+
+
+def cpu_info():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-sample-tokens", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        iters = max(1, min(args.steps, 3))
+        v, sec = run_reference_cpu(args.cpu_sample_tokens, iters)
+        out = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": iters,
+               "warmup": 1, "ms_per_step": sec * 1e3, "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+               "impl": "reference",
+               "config": {"workload": "C2 layer shapes, dense-masked reference path on host cores",
+                          "T_sample": args.cpu_sample_tokens},
+               "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"{args.cpu_sample_tokens} tokens of the C2 layer per step, "
+                                          f"median of {iters}", "cpu": cpu_info()},
+               "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(out))
+        return
+
+    if world > 1:
+        torch.distributed.init_process_group(
+            "nccl", device_id=torch.device("cuda", local_rank),
+            timeout=__import__("datetime").timedelta(seconds=120))
+    out = run_ours(args, rank, world, local_rank)
+    if rank == 0 and not args.no_cpu_baseline:
+        v, sec = run_reference_cpu(args.cpu_sample_tokens, 1)
+        out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"{args.cpu_sample_tokens} tokens of the C2 layer, dense-masked "
+                                         "reference path (all 128 experts per token)",
+                               "cpu": cpu_info()}
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

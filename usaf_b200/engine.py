@@ -1,0 +1,338 @@
+"""Device-resident engine of the MoE expert hot path.
+
+``Projection`` holds one int4 expert tensor (``gate_up_proj [E,2I,H]`` or
+``down_proj [E,H,I]`` in the usaf.quantization layout) and the overlay of its
+trained coordinates.  ``MoEBlock`` owns the per-step workspace and sequences
+the C-ABI kernels for one forward/backward of the block:
+
+  forward : router -> dispatch -> gate_up GEMM + SwiGLU -> down GEMM -> combine
+  backward: combine bwd -> router bwd -> down dX GEMM + SwiGLU bwd
+            -> gate_up dX GEMM -> dX gather; expert grads at the selected
+            coordinates (SDDMM) or dense |grad| for importance.
+
+Reference: usaf/qwen3moe_dml.py:24-86 (block), benchmarks/kaggle_t4_bench.py:
+284-328 (dispatch), usaf/moe_loader.py:226-247, 425-443, 527-631 (weights,
+overlays, stores).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr, stream
+
+
+def _i32(t):
+    return t.to(torch.int32).contiguous()
+
+
+def sort_u32(keys: torch.Tensor, payload: torch.Tensor, descending: bool = False):
+    """Stable device radix sort of int32/uint32 keys (< 2^31 here) with int64 payload."""
+    n = keys.numel()
+    kin = _i32(keys)
+    vin = payload.to(torch.int64).contiguous()
+    kout = torch.empty_like(kin)
+    vout = torch.empty_like(vin)
+    if n == 0:
+        return kout, vout
+    scratch = torch.empty(int(_lib.LIB.usaf_sort_scratch_bytes(n)), dtype=torch.uint8,
+                          device=keys.device)
+    call("usaf_sort_u32", ptr(kin), ptr(vin), n, ptr(kout), ptr(vout), int(descending),
+         ptr(scratch), stream())
+    return kout, vout
+
+
+def build_rowptr(rows: torch.Tensor, n_rows: int) -> torch.Tensor:
+    rows = rows.to(torch.int64).contiguous()
+    out = torch.empty(n_rows + 1, dtype=torch.int32, device=rows.device)
+    call("usaf_build_rowptr", ptr(rows) if rows.numel() else None, rows.numel(), n_rows,
+         ptr(out), stream())
+    return out
+
+
+def topk_desc(vals: torch.Tensor, k: int, idx_map: Optional[torch.Tensor] = None,
+              idx_base: int = 0, want_vals: bool = True):
+    """k largest of a 1-D fp32 tensor, descending; ties in ascending index order."""
+    n = vals.numel()
+    v = vals.contiguous().float()
+    out_i = torch.empty(k, dtype=torch.int64, device=v.device)
+    out_v = torch.empty(k, dtype=torch.float32, device=v.device) if want_vals else None
+    scratch = torch.empty(int(_lib.LIB.usaf_topk_scratch_bytes(n, k)), dtype=torch.uint8,
+                          device=v.device)
+    call("usaf_topk_desc", ptr(v), n, k, ptr(idx_map), idx_base, ptr(out_v), ptr(out_i),
+         ptr(scratch), stream())
+    return out_v, out_i
+
+
+def kth_largest(vals: torch.Tensor, k: int) -> torch.Tensor:
+    n = vals.numel()
+    v = vals.contiguous().float()
+    out = torch.empty(1, dtype=torch.float32, device=v.device)
+    scratch = torch.empty(int(_lib.LIB.usaf_topk_scratch_bytes(n, 1)), dtype=torch.uint8,
+                          device=v.device)
+    call("usaf_kth_largest", ptr(v), n, k, ptr(out), ptr(scratch), stream())
+    return out
+
+
+class Projection:
+    """One int4 expert projection resident in HBM, storage shape [E, R, C].
+
+    ``q/s/z`` are the reference's packed codes, fp16 scales and zeros
+    (usaf/quantization.py:21-85).  ``set_overlay(idx, master)`` installs the
+    trained coordinates (flat indices into [E,R,C]) with their fp32 masters;
+    the GEMMs then see ``dtype(fp16(master))`` at those coordinates, which is
+    ``_get_resident`` + ``sync_resident`` of usaf/moe_loader.py:241-247, 442.
+    """
+
+    def __init__(self, q: torch.Tensor, s: torch.Tensor, z: torch.Tensor, shape,
+                 group_size: int = 128, dtype: torch.dtype = torch.bfloat16):
+        E, R, Cc = (int(x) for x in shape)
+        if Cc % group_size != 0:
+            raise ValueError("int4 groups must not straddle rows (C % group_size != 0)")
+        if E * R * Cc >= 2 ** 31:
+            raise ValueError("projection too large for 32-bit flat indices")
+        self.E, self.R, self.C, self.group_size = E, R, Cc, group_size
+        self.shape = (E, R, Cc)
+        self.q = q.reshape(-1).contiguous()
+        self.s = s.reshape(-1).contiguous()
+        self.z = z.reshape(-1).contiguous()
+        self.dtype = dtype
+        self.device = self.q.device
+        self.n_ov = 0
+        self.row_ptr = self.col = self.val = None
+        self.colT_ptr = self.rowT = self.valT = None
+        self.csr_to_compact = self.compact_to_csr = self.compact_to_csc = None
+        self.scratch = None
+        self._struct = None
+
+    def numel(self) -> int:
+        return self.E * self.R * self.C
+
+    def set_overlay(self, idx: torch.Tensor, master: torch.Tensor):
+        dev = self.device
+        idx = idx.reshape(-1).to(device=dev, dtype=torch.int64)
+        n = idx.numel()
+        self.n_ov = n
+        E, R, Cc = self.E, self.R, self.C
+        ar = torch.arange(n, device=dev, dtype=torch.int64)
+        # CSR: ascending flat index
+        kcsr, pcsr = sort_u32(idx, ar)
+        flat = kcsr.to(torch.int64)
+        self.row_ptr = build_rowptr(flat // Cc, E * R)
+        self.col = _i32(flat % Cc)
+        self.csr_to_compact = _i32(pcsr)
+        self.compact_to_csr = torch.empty(n, dtype=torch.int32, device=dev)
+        self.compact_to_csr[pcsr] = torch.arange(n, device=dev, dtype=torch.int32)
+        # CSC: ascending (e, c, r)
+        e = idx // (R * Cc)
+        r = (idx // Cc) % R
+        c = idx % Cc
+        key = (e * Cc + c) * R + r
+        kcsc, pcsc = sort_u32(key, ar)
+        kc = kcsc.to(torch.int64)
+        self.colT_ptr = build_rowptr(kc // R, E * Cc)
+        self.rowT = _i32(kc % R)
+        self.compact_to_csc = torch.empty(n, dtype=torch.int32, device=dev)
+        self.compact_to_csc[pcsc] = torch.arange(n, device=dev, dtype=torch.int32)
+        self._csc_to_compact = pcsc
+        self.val = torch.empty(n, dtype=torch.float32, device=dev)
+        self.valT = torch.empty(n, dtype=torch.float32, device=dev)
+        self.update_overlay_values(master)
+        self.scratch = torch.empty(max(n, 1), dtype=torch.float32, device=dev)
+        self._struct = None
+
+    def update_overlay_values(self, master: torch.Tensor):
+        ev = master.detach().to(self.device).half().to(self.dtype).float()
+        self.val[self.compact_to_csr.long()] = ev
+        self.valT[self.compact_to_csc.long()] = ev
+
+    def struct(self) -> _lib.QWeight:
+        if self._struct is None:
+            st = _lib.QWeight()
+            st.E, st.R, st.C, st.group_size = self.E, self.R, self.C, self.group_size
+            st.q, st.s, st.z = ptr(self.q), ptr(self.s), ptr(self.z)
+            st.n_ov = self.n_ov
+            if self.n_ov:
+                st.row_ptr, st.col, st.val = ptr(self.row_ptr), ptr(self.col), ptr(self.val)
+                st.colT_ptr, st.rowT, st.valT = ptr(self.colT_ptr), ptr(self.rowT), ptr(self.valT)
+            self._struct = st
+        return self._struct
+
+    def dequant(self, out_dtype=torch.float16) -> torch.Tensor:
+        out = torch.empty(self.numel(), dtype=out_dtype, device=self.device)
+        call("usaf_dequant_int4", ptr(self.q), ptr(self.s), ptr(self.z), self.numel(),
+             self.group_size, _lib.dtype_code(out_dtype), ptr(out), stream())
+        return out.view(self.shape)
+
+
+@dataclass
+class BlockDims:
+    T: int
+    H: int
+    E: int
+    I: int
+    top_k: int
+    norm_topk_prob: bool
+    dtype: torch.dtype
+
+
+class MoEBlock:
+    """Workspace + kernel sequence of one MoE block step (single GPU).
+
+    The pair buffers hold ``P_cap = T * min(E, pair_factor * top_k)`` routed
+    (token, expert) pairs; threshold ties can route a token to more than
+    top_k experts, and a batch that overflows the buffer is reported through
+    the device error word (read by :meth:`check`).
+    """
+
+    def __init__(self, dims: BlockDims, device, pair_factor: int = 2):
+        self.d = dims
+        T, H, E, I = dims.T, dims.H, dims.E, dims.I
+        self.device = torch.device(device)
+        self.dt = dims.dtype
+        self.dtc = _lib.dtype_code(dims.dtype)
+        self.P_cap = T * min(E, pair_factor * dims.top_k)
+        dev, dt, Pc = self.device, self.dt, self.P_cap
+        i32 = dict(dtype=torch.int32, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        act = dict(dtype=dt, device=dev)
+        nch = (T + 255) // 256
+        self.tok_cnt = torch.zeros(max(T, 1), **i32)
+        self.tok_off = torch.zeros(T + 1, **i32)
+        self.expert_cnt = torch.zeros(E, **i32)
+        self.expert_off = torch.zeros(E + 1, **i32)
+        self.seg_tok = torch.zeros(Pc, **i32)
+        self.seg_pair = torch.zeros(Pc, **i32)
+        self.seg_w = torch.zeros(Pc, **f32)
+        self.pair_exp = torch.zeros(Pc, **i32)
+        self.pair_slot = torch.zeros(Pc, **i32)
+        self.n_pairs = torch.zeros(1, **i32)
+        self.chunk_cnt = torch.zeros(max(nch * E, 1), **i32)
+        self.err = torch.zeros(1, **i32)
+        self.logits = torch.empty(T, E, **f32)
+        self.probs = torch.empty(T, E, **f32)
+        self.wsum = torch.empty(T, **f32)
+        self.weights = torch.empty(T, E, **act)
+        self.x_perm = torch.empty(Pc, H, **act)
+        self.gu = torch.empty(Pc, 2 * I, **act)
+        self.h = torch.empty(Pc, I, **act)
+        self.y_seg = torch.empty(Pc, H, **act)
+        self.y = torch.empty(T, H, **act)
+        self.dcur = torch.empty(Pc, H, **act)
+        self.dw_pair = torch.empty(Pc, **f32)
+        self.dgu = torch.empty(Pc, 2 * I, **act)
+        self.dx_seg = torch.empty(Pc, H, **act)
+        self.dlogits = torch.empty(T, E, **f32)
+        self.dx_acc = torch.empty(T, H, **f32)
+        self.dx = torch.empty(T, H, **act)
+        self.dw_r = torch.empty(E, H, **act)
+        self.plan = _lib.RoutePlan()
+        p = self.plan
+        p.T, p.E, p.P_cap = T, E, Pc
+        for name in ("tok_cnt", "tok_off", "expert_cnt", "expert_off", "seg_tok", "seg_pair",
+                     "seg_w", "pair_exp", "pair_slot", "n_pairs", "chunk_cnt", "err"):
+            setattr(p, name, ptr(getattr(self, name)))
+
+    # ---------------------------------------------------------------- fwd ---
+    def forward(self, x: torch.Tensor, w_r: torch.Tensor, gu: Projection, dn: Projection):
+        d = self.d
+        assert x.shape == (d.T, d.H) and x.dtype == self.dt and x.is_contiguous()
+        st = stream()
+        call("usaf_router_fwd", ptr(x), ptr(w_r), self.dtc, d.T, d.H, d.E, d.top_k,
+             int(d.norm_topk_prob), ptr(self.logits), ptr(self.probs), ptr(self.wsum),
+             ptr(self.weights), st)
+        call("usaf_dispatch", self.plan, ptr(self.weights), ptr(x), self.dtc, d.H,
+             ptr(self.x_perm), st)
+        call("usaf_expert_gate_up_fwd", self.plan, gu.struct(), ptr(self.x_perm), self.dtc,
+             ptr(self.gu), ptr(self.h), st)
+        call("usaf_expert_down_fwd", self.plan, dn.struct(), ptr(self.h), self.dtc,
+             ptr(self.y_seg), st)
+        call("usaf_combine", self.plan, ptr(self.y_seg), self.dtc, d.H, ptr(self.y), st)
+        return self.y
+
+    # ---------------------------------------------------------------- bwd ---
+    def backward(self, dy: torch.Tensor, x: torch.Tensor, w_r: torch.Tensor, gu: Projection,
+                 dn: Projection):
+        d = self.d
+        assert dy.shape == (d.T, d.H) and dy.dtype == self.dt and dy.is_contiguous()
+        st = stream()
+        call("usaf_combine_bwd", self.plan, ptr(dy), ptr(self.y_seg), self.dtc, d.H,
+             ptr(self.dcur), ptr(self.dw_pair), st)
+        call("usaf_router_bwd", self.plan, ptr(x), ptr(w_r), self.dtc, d.H,
+             int(d.norm_topk_prob), ptr(self.probs), ptr(self.wsum), ptr(self.weights),
+             ptr(self.dw_pair), ptr(self.dlogits), ptr(self.dw_r), ptr(self.dx_acc), st)
+        call("usaf_expert_down_bwd", self.plan, dn.struct(), ptr(self.dcur), ptr(self.gu),
+             self.dtc, ptr(self.dgu), st)
+        call("usaf_expert_gate_up_bwd", self.plan, gu.struct(), ptr(self.dgu), self.dtc,
+             ptr(self.dx_seg), st)
+        call("usaf_gather_dx", self.plan, ptr(self.dx_seg), ptr(self.dx_acc), self.dtc, d.H,
+             ptr(self.dx), st)
+        return self.dx, self.dw_r
+
+    # ------------------------------------------------- expert weight grads ---
+    def sparse_grads(self, gu: Projection, dn: Projection, compact_gu: torch.Tensor,
+                     compact_dn: torch.Tensor, scale: float = 1.0):
+        """compact[pos] += scale * dtype(dW[e,r,c]) at every overlay coordinate."""
+        st = stream()
+        if gu.n_ov:
+            call("usaf_sparse_dw", self.plan, gu.struct(), ptr(self.dgu), ptr(self.x_perm),
+                 self.dtc, ptr(gu.csr_to_compact), scale, ptr(compact_gu), ptr(gu.scratch), st)
+        if dn.n_ov:
+            call("usaf_sparse_dw", self.plan, dn.struct(), ptr(self.dcur), ptr(self.h),
+                 self.dtc, ptr(dn.csr_to_compact), scale, ptr(compact_dn), ptr(dn.scratch), st)
+
+    def dense_abs_grad(self, which: str) -> torch.Tensor:
+        """|dW| of every expert of one projection as fp32 [E, R, C] (importance)."""
+        d = self.d
+        if which == "gate_up_proj":
+            R, Cc, gout, gin = 2 * d.I, d.H, self.dgu, self.x_perm
+        else:
+            R, Cc, gout, gin = d.H, d.I, self.dcur, self.h
+        out = torch.empty(d.E, R, Cc, dtype=torch.float32, device=self.device)
+        call("usaf_expert_dense_dw", self.plan, R, Cc, ptr(gout), ptr(gin), self.dtc, ptr(out),
+             stream())
+        return out
+
+    def check(self):
+        """Raise if a kernel flagged an error (syncs the stream)."""
+        e = int(self.err.item())
+        if e:
+            self.err.zero_()
+            msgs = []
+            if e & _lib.ERR_PAIR_OVERFLOW:
+                msgs.append(f"routed pairs exceed the pair buffer ({self.P_cap})")
+            if e & _lib.ERR_WAIT_TIMEOUT:
+                msgs.append("a device-side wait timed out")
+            if e & _lib.ERR_BAD_INDEX:
+                msgs.append("an out-of-range index was skipped")
+            raise _lib.UsafError("; ".join(msgs))
+
+    def n_pairs_host(self) -> int:
+        return int(self.n_pairs.item())
+
+
+def sparse_adam_compact(master, m, v, grad, step, lr, betas, eps, weight_decay, proj=None,
+                        grad_div=1.0, dtype=torch.bfloat16):
+    """One fused SparseAdam step (usaf/sparse_optim.py:86-134, compact mode),
+    writing the new overlay values of ``proj`` (sync_resident) in the same pass."""
+    n = master.numel()
+    call("usaf_sparse_adam", n, ptr(master), ptr(m), ptr(v), ptr(grad), float(grad_div),
+         int(step), float(lr), float(betas[0]), float(betas[1]), float(eps),
+         float(weight_decay), _lib.dtype_code(dtype),
+         ptr(proj.val) if proj is not None else None,
+         ptr(proj.compact_to_csr) if proj is not None else None,
+         ptr(proj.valT) if proj is not None else None,
+         ptr(proj.compact_to_csc) if proj is not None else None, stream())
+
+
+def sparse_adam_gather(param, grad, idx, m, v, step, lr, betas, eps, weight_decay,
+                       grad_div=1.0):
+    """SparseAdam gather/scatter mode (usaf/sparse_optim.py:110-134) on a
+    dense parameter (the router)."""
+    n = idx.numel()
+    call("usaf_sparse_adam_gather", n, ptr(idx), ptr(param), ptr(grad),
+         _lib.dtype_code(param.dtype), float(grad_div), ptr(m), ptr(v), int(step), float(lr),
+         float(betas[0]), float(betas[1]), float(eps), float(weight_decay), stream())
