@@ -117,7 +117,8 @@ def test_router_ties_fixture(dev, golden_dir):
     pr = torch.empty(T, E, device=dev)
     ws = torch.empty(T, device=dev)
     wt = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
-    _lib.call("usaf_router_fwd", _lib.ptr(x.to(dev)), _lib.ptr(w_r.to(dev)), _lib.BF16, T, H, E,
+    xd, wd = x.to(dev), w_r.to(dev)  # device copies must outlive the launch
+    _lib.call("usaf_router_fwd", _lib.ptr(xd), _lib.ptr(wd), _lib.BF16, T, H, E,
               t["k"], 1, _lib.ptr(lg), _lib.ptr(pr), _lib.ptr(ws), _lib.ptr(wt), _lib.stream())
     assert torch.equal(wt.cpu() != 0, t["weights"] != 0)
     assert int((wt.cpu() != 0).sum(1).max()) > t["k"]
@@ -132,7 +133,8 @@ def test_dispatch_matches_reference_indices(dev, golden_dir):
     T, E = w.shape
     blk = MoEBlock(BlockDims(T, 64, E, 128, 4, True, torch.bfloat16), dev)
     x = torch.randn(T, 64).to(torch.bfloat16).to(dev)
-    _lib.call("usaf_dispatch", blk.plan, _lib.ptr(w.to(dev)), _lib.ptr(x), _lib.BF16, 64,
+    wd = w.to(dev)
+    _lib.call("usaf_dispatch", blk.plan, _lib.ptr(wd), _lib.ptr(x), _lib.BF16, 64,
               _lib.ptr(blk.x_perm), _lib.stream())
     P = blk.n_pairs_host()
     assert P == g["dispatch.tok_idx"].numel()

@@ -1,13 +1,399 @@
-// tcgen05 grouped expert GEMMs -- placeholder until the sm_100a kernels land.
+// tcgen05 grouped expert GEMMs over int4 weights (sm_100a).
+//
+// One CTA computes D[128 weight rows x up to 384 tokens] of one expert:
+//   * A (weights) is dequantized on the fly by 4 producer warps: each thread
+//     owns one TMEM lane (= one weight row), loads its row's packed int4
+//     codes with 128-bit loads (prefetched 3 k-blocks ahead), computes
+//     fp16(fp16(q*s)+z) -> bf16 in registers (the reference's rounding),
+//     patches trained coordinates from the CSR overlay, and writes the 64-wide
+//     k-block straight into TMEM with tcgen05.st -- the dequantized weights
+//     never touch shared memory or HBM;
+//   * B (tokens of the expert's segment, K-major) arrives in shared memory by
+//     TMA with the 128-byte swizzle (plain per-CTA loads, no multicast);
+//   * one thread issues tcgen05.mma (kind::f16, M=128, N<=128 per sub-tile,
+//     A from TMEM, B from SMEM) into fp32 TMEM accumulators; tcgen05.commit
+//     frees pipeline stages and finally signals the epilogue;
+//   * the epilogue warps read the accumulators (tcgen05.ld), round to bf16,
+//     transpose through shared memory and write token rows with 16-byte
+//     stores; in gate_up mode the CTA's 128 rows are 64 gate rows and the
+//     matching 64 up rows, so SwiGLU is fused here.
+// TMEM: columns [0,384) accumulators (3 token sub-tiles), [384,512) four A
+// stages of 32 columns (64 bf16 of K per lane).  All waits are bounded.
+#include <cudaTypedefs.h>
+
 #include "gemm_tc.cuh"
+#include "tc_common.cuh"
 
 namespace usaf {
-bool tc_supported_gate_up(const usaf_qweight *) { return false; }
-bool tc_supported_down(const usaf_qweight *) { return false; }
+using namespace tc;
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kBK = 64;
+constexpr int kSub = 128;
+constexpr int kMaxSub = 3;
+constexpr int kMaxTok = kSub * kMaxSub;          // 384 tokens per CTA
+constexpr int kSubBytes = kSub * kBK * 2;        // 16 KB per TMA box
+constexpr int kStageBytes = kMaxSub * kSubBytes; // 48 KB per stage
+constexpr int kAcol = kMaxTok;                   // first TMEM column of the A stages
+constexpr int kThreads = 256;
+constexpr int kStageLd = 136;                    // epilogue staging row stride (elements)
+
+enum : int { MODE_GATE_UP = 0, MODE_DOWN = 1 };
+
+struct alignas(8) TcShared {
+    uint64_t full_b[kStages];
+    uint64_t full_a[kStages];
+    uint64_t empty[kStages];
+    uint64_t acc;
+    uint32_t tmem_base;
+    int e, t0, ntok, seg0;
+    int abort_flag;
+};
+
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(TcShared) + 1024;
+
+// time-bounded wait that ignores the abort flag (used to drain in-flight work)
+__device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, int *err) {
+    uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > kWaitBudgetNs) {
+            atomicOr(err, USAF_ERR_WAIT_TIMEOUT);
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void dequant_block(uint4 a, uint4 b, uint16_t s_bits, uint16_t z_bits,
+                                              uint32_t (&r)[32]) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const __half2 s2 = __half2half2(__ushort_as_half(s_bits));
+    const __half2 z2 = __half2half2(__ushort_as_half(z_bits));
+    const __half2 magic = __half2half2(__ushort_as_half((unsigned short)0x6400));  // 1024
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        uint32_t byte = (w[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+        uint32_t u = (byte & 0xFu) | ((byte & 0xF0u) << 12) | 0x64006400u;
+        __half2 c = __hsub2(*reinterpret_cast<__half2 *>(&u), magic);  // exact codes (lo, hi)
+        __half2 v = __hadd2_rn(__hmul2_rn(c, s2), z2);                  // fp16(fp16(q*s)+z)
+        float2 f = __half22float2(v);
+        __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
+        r[j] = *reinterpret_cast<uint32_t *>(&bb);
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_fwd_kernel(const __grid_constant__ CUtensorMap tmap_b, usaf_route_plan pl, usaf_qweight w,
+                  __nv_bfloat16 *__restrict__ out0, __nv_bfloat16 *__restrict__ out1) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *sbase = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    TcShared &S = *reinterpret_cast<TcShared *>(sbase + (size_t)kStages * kStageBytes);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int K = w.C, R = w.R;
+    const int nk = K / kBK;
+    int *err = pl.err;
+
+    if (tid == 0) {
+        // token tile of this CTA: experts are cut into ceil(cnt/384) balanced tiles
+        int tile = blockIdx.y, acc_t = 0, e = -1, t0 = 0, ntok = 0;
+        for (int e_ = 0; e_ < pl.E; ++e_) {
+            int cnt = pl.expert_cnt[e_];
+            if (cnt == 0) continue;
+            int ntt = (cnt + kMaxTok - 1) / kMaxTok;
+            if (tile < acc_t + ntt) {
+                int tt = tile - acc_t;
+                int per = (((cnt + ntt - 1) / ntt) + 15) & ~15;
+                e = e_;
+                t0 = tt * per;
+                ntok = min(per, cnt - t0);
+                break;
+            }
+            acc_t += ntt;
+        }
+        S.e = e;
+        S.t0 = t0;
+        S.ntok = ntok;
+        S.seg0 = e >= 0 ? pl.expert_off[e] : 0;
+        S.abort_flag = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&S.full_b[s], 1);
+            mbar_init(&S.full_a[s], 128);
+            mbar_init(&S.empty[s], 1);
+        }
+        mbar_init(&S.acc, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int e = S.e;
+    if (e < 0) return;  // whole CTA leaves together: no TMEM, no barriers in flight
+    const int t0 = S.t0, ntok = S.ntok, seg0 = S.seg0;
+    const int nsub = (ntok + kSub - 1) / kSub;
+    const int row0 = seg0 + t0;  // first token row (slot) of this tile
+    volatile int *abort_flag = &S.abort_flag;
+
+    if (warp == 1) tmem_alloc(&S.tmem_base, 512);
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = S.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (tokens) ----------------
+        if (lane == 0) {
+            prefetch_tmap(&tmap_b);
+            int last_kb[kStages];
+            for (int s = 0; s < kStages; ++s) last_kb[s] = -1;
+            for (int kb = 0; kb < nk; ++kb) {
+                int st = kb % kStages;
+                uint32_t par = ((kb / kStages) & 1) ^ 1;
+                if (!mbar_wait(&S.empty[st], par, abort_flag, err)) break;
+                mbar_arrive_expect_tx(&S.full_b[st], (uint32_t)(nsub * kSubBytes));
+                unsigned char *dst = sbase + (size_t)st * kStageBytes;
+                for (int j = 0; j < nsub; ++j)
+                    tma_load_2d(dst + j * kSubBytes, &tmap_b, &S.full_b[st], kb * kBK, row0 + j * kSub);
+                last_kb[st] = kb;
+            }
+            if (*abort_flag) {
+                for (int s = 0; s < kStages; ++s)
+                    if (last_kb[s] >= 0) drain_wait(&S.full_b[s], (last_kb[s] / kStages) & 1, err);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            uint32_t idesc[kMaxSub];
+            for (int j = 0; j < kMaxSub; ++j) {
+                int n = min(kSub, ntok - j * kSub);
+                n = n < 16 ? 16 : ((n + 15) & ~15);
+                idesc[j] = idesc_bf16(128, n);
+            }
+            for (int kb = 0; kb < nk; ++kb) {
+                int st = kb % kStages;
+                uint32_t par = (kb / kStages) & 1;
+                if (!mbar_wait(&S.full_b[st], par, abort_flag, err)) break;
+                if (!mbar_wait(&S.full_a[st], par, abort_flag, err)) break;
+                tc_fence_after();
+                uint32_t bst = smem_u32(sbase + (size_t)st * kStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    uint32_t a_t = tbase + kAcol + st * 32 + kk * 8;
+                    for (int j = 0; j < nsub; ++j) {
+                        uint64_t bd = smem_desc_sw128(bst + j * kSubBytes + kk * 32);
+                        mma_ts(tbase + j * kSub, a_t, bd, idesc[j], (kb | kk) != 0);
+                    }
+                }
+                mma_commit(&S.empty[st]);
+            }
+            mma_commit(&S.acc);
+        }
+    } else if (warp >= 4) {
+        // ---------------- dequant producers, then epilogue ----------------
+        const int t = tid - 128;                 // TMEM lane = weight row of this tile
+        const uint32_t lane_base = (uint32_t)(warp & 3) * 32;
+        int row_st;                              // storage row inside the expert
+        int j0 = 0, h0 = 0;
+        const int I = R / 2;
+        if (MODE == MODE_GATE_UP) {
+            j0 = blockIdx.x * 64;
+            row_st = t < 64 ? j0 + t : I + j0 + (t - 64);
+        } else {
+            h0 = blockIdx.x * 128;
+            row_st = h0 + t;
+        }
+        const int64_t grow = (int64_t)e * R + row_st;
+        const uint4 *qrow = reinterpret_cast<const uint4 *>(w.q + grow * (K / 2));
+        const int64_t gbase = grow * (int64_t)K;
+        const uint16_t *sz_s = w.s, *sz_z = w.z;
+        const int gs = w.group_size;
+        // overlay cursor of this row (CSR sorted by column)
+        int cur = 0, cend = 0, ncol = 0x7fffffff;
+        float nval = 0.0f;
+        if (w.n_ov > 0) {
+            cur = w.row_ptr[grow];
+            cend = w.row_ptr[grow + 1];
+            if (cur < cend) { ncol = w.col[cur]; nval = w.val[cur]; }
+        }
+        uint4 qa[4], qb[4];
+        uint16_t ss[4], zz[4];
+        auto load = [&](int kb, uint4 &a, uint4 &b, uint16_t &s_, uint16_t &z_) {
+            a = __ldg(qrow + kb * 2);
+            b = __ldg(qrow + kb * 2 + 1);
+            int64_t g = (gbase + (int64_t)kb * kBK) / gs;
+            s_ = __ldg(sz_s + g);
+            z_ = __ldg(sz_z + g);
+        };
+#pragma unroll
+        for (int d = 0; d < 3; ++d)
+            if (d < nk) load(d, qa[d], qb[d], ss[d], zz[d]);
+        bool ok = true;
+        for (int kb0 = 0; kb0 < nk && ok; kb0 += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int kb = kb0 + u;
+                if (kb < nk && ok) {
+                    if (kb + 3 < nk) load(kb + 3, qa[(u + 3) & 3], qb[(u + 3) & 3], ss[(u + 3) & 3], zz[(u + 3) & 3]);
+                    const int st = kb % kStages;
+                    const uint32_t par = ((kb / kStages) & 1) ^ 1;
+                    uint32_t r[32];
+                    dequant_block(qa[u], qb[u], ss[u], zz[u], r);
+                    const int k0 = kb * kBK;
+                    while (ncol < k0 + kBK) {
+                        const int c = ncol - k0;
+                        const uint32_t vb = __bfloat16_as_ushort(__float2bfloat16_rn(nval));
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (i == (c >> 1))
+                                r[i] = (c & 1) ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
+                        ++cur;
+                        if (cur < cend) { ncol = w.col[cur]; nval = w.val[cur]; }
+                        else ncol = 0x7fffffff;
+                    }
+                    if (!mbar_wait(&S.empty[st], par, abort_flag, err)) { ok = false; break; }
+                    tc_fence_after();
+                    tmem_st_32x32b_x32(tbase + (lane_base << 16) + kAcol + st * 32, r);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&S.full_a[st]);
+                }
+            }
+        }
+        // ---- epilogue ----
+        drain_wait(&S.acc, 0, err);
+        tc_fence_after();
+        fence_proxy_async();
+        __nv_bfloat16 *stg = reinterpret_cast<__nv_bfloat16 *>(sbase);  // [32 tokens][kStageLd]
+        if (!*abort_flag) {
+            for (int c0 = 0; c0 < ntok; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tbase + (lane_base << 16) + c0, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    stg[i * kStageLd + t] = __float2bfloat16_rn(__uint_as_float(v[i]));
+                named_bar_sync(1, 128);
+                if (MODE == MODE_DOWN) {
+                    for (int item = t; item < 32 * 16; item += 128) {
+                        const int j = item >> 4, sg = item & 15;
+                        if (c0 + j < ntok) {
+                            const int64_t slot = row0 + c0 + j;
+                            uint4 val = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
+                            *reinterpret_cast<uint4 *>(out0 + slot * R + h0 + sg * 8) = val;
+                        }
+                    }
+                } else {
+                    for (int item = t; item < 32 * 8; item += 128) {
+                        const int j = item >> 3, sg = item & 7;
+                        if (c0 + j < ntok) {
+                            const int64_t slot = row0 + c0 + j;
+                            uint4 gv = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
+                            uint4 uv = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + 64 + sg * 8);
+                            const __nv_bfloat16 *g8 = reinterpret_cast<const __nv_bfloat16 *>(&gv);
+                            const __nv_bfloat16 *u8 = reinterpret_cast<const __nv_bfloat16 *>(&uv);
+                            __align__(16) __nv_bfloat16 h8[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                float g = __bfloat162float(g8[q]);
+                                float sg_ = __bfloat162float(__float2bfloat16_rn(
+                                    __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+                                h8[q] = __float2bfloat16_rn(__fmul_rn(sg_, __bfloat162float(u8[q])));
+                            }
+                            *reinterpret_cast<uint4 *>(out0 + slot * R + j0 + sg * 8) = gv;
+                            *reinterpret_cast<uint4 *>(out0 + slot * R + I + j0 + sg * 8) = uv;
+                            *reinterpret_cast<uint4 *>(out1 + slot * I + j0 + sg * 8) =
+                                *reinterpret_cast<const uint4 *>(h8);
+                        }
+                    }
+                }
+                named_bar_sync(1, 128);
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// ---- host: tensor maps ------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// row-major bf16 matrix [rows, cols] -> tiles of 128 rows x 64 cols, 128-byte swizzle
+bool make_tmap_rows(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (cols * 2) % 16) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kSub};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int MODE>
+int launch_fwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *act,
+               __nv_bfloat16 *out0, __nv_bfloat16 *out1, cudaStream_t st) {
+    CUtensorMap tm;
+    if (!make_tmap_rows(&tm, act, pl->P_cap, w->C)) return USAF_EUNSUPPORTED;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(tc_fwd_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemBytes) != cudaSuccess)
+            return USAF_ECUDA;
+        attr_set = true;
+    }
+    int nrb = MODE == MODE_GATE_UP ? (w->R / 2) / 64 : w->R / 128;
+    int tiles = pl->P_cap / kMaxTok + 1 + pl->E;
+    dim3 grid(nrb, tiles);
+    tc_fwd_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(tm, *pl, *w, out0, out1);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
+}
+
+bool shape_ok_common(const usaf_qweight *w) {
+    return w->C % kBK == 0 && w->group_size % kBK == 0 && w->C % 32 == 0 &&
+           encode_fn() != nullptr;
+}
+
+}  // namespace
+
+bool tc_supported_gate_up(const usaf_qweight *w) { return shape_ok_common(w) && (w->R / 2) % 64 == 0 && w->R % 2 == 0; }
+bool tc_supported_down(const usaf_qweight *w) { return shape_ok_common(w) && w->R % 128 == 0; }
 bool tc_supported_down_bwd(const usaf_qweight *) { return false; }
 bool tc_supported_gate_up_bwd(const usaf_qweight *) { return false; }
-int tc_gate_up_fwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *, __nv_bfloat16 *, __nv_bfloat16 *, cudaStream_t) { return USAF_EUNSUPPORTED; }
-int tc_down_fwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *, __nv_bfloat16 *, cudaStream_t) { return USAF_EUNSUPPORTED; }
-int tc_down_bwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *, const __nv_bfloat16 *, __nv_bfloat16 *, cudaStream_t) { return USAF_EUNSUPPORTED; }
-int tc_gate_up_bwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *, __nv_bfloat16 *, cudaStream_t) { return USAF_EUNSUPPORTED; }
+
+int tc_gate_up_fwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *x_perm,
+                   __nv_bfloat16 *gu, __nv_bfloat16 *h, cudaStream_t st) {
+    return launch_fwd<MODE_GATE_UP>(pl, w, x_perm, gu, h, st);
+}
+int tc_down_fwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *h,
+                __nv_bfloat16 *y_seg, cudaStream_t st) {
+    return launch_fwd<MODE_DOWN>(pl, w, h, y_seg, nullptr, st);
+}
+int tc_down_bwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *,
+                const __nv_bfloat16 *, __nv_bfloat16 *, cudaStream_t) {
+    return USAF_EUNSUPPORTED;
+}
+int tc_gate_up_bwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *,
+                   __nv_bfloat16 *, cudaStream_t) {
+    return USAF_EUNSUPPORTED;
+}
+
 }  // namespace usaf

@@ -45,8 +45,9 @@ def dequantize_4bit(q_int4: torch.Tensor, scale: torch.Tensor, zero: torch.Tenso
                     group_size: int = 128, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
     numel = _numel(shape)
     out = torch.empty(numel, dtype=out_dtype, device=q_int4.device)
-    _lib.call("usaf_dequant_int4", _lib.ptr(q_int4.contiguous()),
-              _lib.ptr(scale.contiguous()), _lib.ptr(zero.contiguous()), numel, group_size,
+    # keep the contiguous copies alive until the kernel is enqueued
+    q, s, z = q_int4.contiguous(), scale.contiguous(), zero.contiguous()
+    _lib.call("usaf_dequant_int4", _lib.ptr(q), _lib.ptr(s), _lib.ptr(z), numel, group_size,
               _lib.dtype_code(out_dtype), _lib.ptr(out), _lib.stream())
     return out.view(tuple(shape))
 
