@@ -46,13 +46,16 @@ struct alignas(8) TcShared {
     uint64_t full_b[kStages];
     uint64_t full_a[kStages];
     uint64_t empty[kStages];
-    uint64_t acc;
+    uint64_t acc;        // accumulators ready (tcgen05.commit)
+    uint64_t acc_empty;  // accumulators drained by the epilogue (128 arrivals)
     uint32_t tmem_base;
-    int e, t0, ntok, seg0;
     int abort_flag;
 };
 
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + sizeof(TcShared) + 1024;
+constexpr size_t kStgBytes = (size_t)32 * kStageLd * 2;  // epilogue staging tile
+// stages + epilogue staging + shared block + per-expert tile prefix / counts (E <= 1024)
+constexpr size_t kSmemBytes =
+    (size_t)kStages * kStageBytes + kStgBytes + sizeof(TcShared) + 8 * 1025 + 1024;
 
 // time-bounded wait that ignores the abort flag (used to drain in-flight work)
 __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, int *err) {
@@ -83,56 +86,106 @@ __device__ __forceinline__ void dequant_block(uint4 a, uint4 b, uint16_t s_bits,
     }
 }
 
+// Work item = (token tile, row block); tile t of expert e covers tokens
+// [t0, t0+ntok) of e's segment.  Consecutive work items share a token tile
+// so its rows are reused from L2 across row blocks.
+struct TileMap {
+    int n_tiles;
+};
+
+__device__ __forceinline__ void decode_tile(const int *tile_off, const int *cnts, int E, int tile,
+                                            int &e, int &t0, int &ntok) {
+    int lo = 0, hi = E;  // first expert with tile_off[e+1] > tile
+    while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if (tile_off[mid + 1] > tile) hi = mid;
+        else lo = mid + 1;
+    }
+    e = lo;
+    int cnt = cnts[e];
+    int ntt = tile_off[e + 1] - tile_off[e];
+    int tt = tile - tile_off[e];
+    int per = (((cnt + ntt - 1) / ntt) + 15) & ~15;
+    t0 = tt * per;
+    ntok = min(per, cnt - t0);
+}
+
+// Replace element c (0..63) of a packed bf16x2 block with the bf16 bits vb.
+// A predicated select per register keeps r[] in registers (an indexed write
+// would move the whole block to local memory).
+__device__ __forceinline__ void patch_elem(uint32_t (&r)[32], int c, uint32_t vb) {
+    const uint32_t pi = (uint32_t)c >> 1;
+    const bool hi = c & 1;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t cand = hi ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
+        asm volatile("{\n .reg .pred p;\n setp.eq.u32 p, %1, %2;\n selp.b32 %0, %3, %0, p;\n}\n"
+                     : "+r"(r[i])
+                     : "r"(pi), "r"((uint32_t)i), "r"(cand));
+    }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmap_b, usaf_route_plan pl, usaf_qweight w,
-                  __nv_bfloat16 *__restrict__ out0, __nv_bfloat16 *__restrict__ out1) {
+                  __nv_bfloat16 *__restrict__ out0, __nv_bfloat16 *__restrict__ out1, int nrb) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *sbase = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    TcShared &S = *reinterpret_cast<TcShared *>(sbase + (size_t)kStages * kStageBytes);
+    __nv_bfloat16 *stg = reinterpret_cast<__nv_bfloat16 *>(sbase + (size_t)kStages * kStageBytes);
+    TcShared &S = *reinterpret_cast<TcShared *>(sbase + (size_t)kStages * kStageBytes + kStgBytes);
+    int *tile_off = reinterpret_cast<int *>(&S + 1);         // [E+1]
+    int *cnts = tile_off + (pl.E + 1);                        // [E]
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int K = w.C, R = w.R;
+    const int K = w.C, R = w.R, E = pl.E;
     const int nk = K / kBK;
     int *err = pl.err;
 
-    if (tid == 0) {
-        // token tile of this CTA: experts are cut into ceil(cnt/384) balanced tiles
-        int tile = blockIdx.y, acc_t = 0, e = -1, t0 = 0, ntok = 0;
-        for (int e_ = 0; e_ < pl.E; ++e_) {
-            int cnt = pl.expert_cnt[e_];
-            if (cnt == 0) continue;
-            int ntt = (cnt + kMaxTok - 1) / kMaxTok;
-            if (tile < acc_t + ntt) {
-                int tt = tile - acc_t;
-                int per = (((cnt + ntt - 1) / ntt) + 15) & ~15;
-                e = e_;
-                t0 = tt * per;
-                ntok = min(per, cnt - t0);
-                break;
+    // ---- per-expert tile prefix (block-wide scan, E <= 1024) ----
+    {
+        __shared__ int warp_tot[kThreads / 32];
+        int c4[4], n4[4], mine = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int e_ = tid * 4 + q;
+            c4[q] = e_ < E ? pl.expert_cnt[e_] : 0;
+            n4[q] = (c4[q] + kMaxTok - 1) / kMaxTok;
+            mine += n4[q];
+        }
+        int x = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_tot[warp] = x;
+        __syncthreads();
+        int run = 0;
+        for (int i = 0; i < warp; ++i) run += warp_tot[i];
+        run += x - mine;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            int e_ = tid * 4 + q;
+            if (e_ < E) { tile_off[e_] = run; cnts[e_] = c4[q]; }
+            run += n4[q];
+        }
+        if (tid == kThreads - 1) tile_off[E] = run;
+        if (tid == 0) {
+            S.abort_flag = 0;
+            for (int st = 0; st < kStages; ++st) {
+                mbar_init(&S.full_b[st], 1);
+                mbar_init(&S.full_a[st], 128);
+                mbar_init(&S.empty[st], 1);
             }
-            acc_t += ntt;
+            mbar_init(&S.acc, 1);
+            mbar_init(&S.acc_empty, 128);
+            fence_barrier_init();
         }
-        S.e = e;
-        S.t0 = t0;
-        S.ntok = ntok;
-        S.seg0 = e >= 0 ? pl.expert_off[e] : 0;
-        S.abort_flag = 0;
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&S.full_b[s], 1);
-            mbar_init(&S.full_a[s], 128);
-            mbar_init(&S.empty[s], 1);
-        }
-        mbar_init(&S.acc, 1);
-        fence_barrier_init();
     }
     __syncthreads();
-    const int e = S.e;
-    if (e < 0) return;  // whole CTA leaves together: no TMEM, no barriers in flight
-    const int t0 = S.t0, ntok = S.ntok, seg0 = S.seg0;
-    const int nsub = (ntok + kSub - 1) / kSub;
-    const int row0 = seg0 + t0;  // first token row (slot) of this tile
+    const int n_work = tile_off[E] * nrb;
+    if ((int)blockIdx.x >= n_work) return;  // whole CTA leaves before any TMEM / async work
     volatile int *abort_flag = &S.abort_flag;
 
     if (warp == 1) tmem_alloc(&S.tmem_base, 512);
@@ -144,131 +197,146 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- TMA producer (tokens) ----------------
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
-            int last_kb[kStages];
-            for (int s = 0; s < kStages; ++s) last_kb[s] = -1;
-            for (int kb = 0; kb < nk; ++kb) {
-                int st = kb % kStages;
-                uint32_t par = ((kb / kStages) & 1) ^ 1;
-                if (!mbar_wait(&S.empty[st], par, abort_flag, err)) break;
-                mbar_arrive_expect_tx(&S.full_b[st], (uint32_t)(nsub * kSubBytes));
-                unsigned char *dst = sbase + (size_t)st * kStageBytes;
-                for (int j = 0; j < nsub; ++j)
-                    tma_load_2d(dst + j * kSubBytes, &tmap_b, &S.full_b[st], kb * kBK, row0 + j * kSub);
-                last_kb[st] = kb;
+            int g = 0;  // global k-block counter (shared sequence with the other roles)
+            int last_g = -1;  // last issued k-block; stages of the final kStages are in flight
+            for (int work = blockIdx.x; work < n_work && !*abort_flag; work += gridDim.x) {
+                int e, t0, ntok;
+                decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+                const int row0 = pl.expert_off[e] + t0;
+                const int nsub = (ntok + kSub - 1) / kSub;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int st = g % kStages;
+                    if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) break;
+                    mbar_arrive_expect_tx(&S.full_b[st], (uint32_t)(nsub * kSubBytes));
+                    unsigned char *dst = sbase + (size_t)st * kStageBytes;
+                    for (int j = 0; j < nsub; ++j)
+                        tma_load_2d(dst + j * kSubBytes, &tmap_b, &S.full_b[st], kb * kBK, row0 + j * kSub);
+                    last_g = g;
+                }
             }
             if (*abort_flag) {
-                for (int s = 0; s < kStages; ++s)
-                    if (last_kb[s] >= 0) drain_wait(&S.full_b[s], (last_kb[s] / kStages) & 1, err);
+                for (int gg = max(0, last_g - kStages + 1); gg <= last_g; ++gg)
+                    drain_wait(&S.full_b[gg % kStages], (gg / kStages) & 1, err);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            uint32_t idesc[kMaxSub];
-            for (int j = 0; j < kMaxSub; ++j) {
-                int n = min(kSub, ntok - j * kSub);
-                n = n < 16 ? 16 : ((n + 15) & ~15);
-                idesc[j] = idesc_bf16(128, n);
-            }
-            for (int kb = 0; kb < nk; ++kb) {
-                int st = kb % kStages;
-                uint32_t par = (kb / kStages) & 1;
-                if (!mbar_wait(&S.full_b[st], par, abort_flag, err)) break;
-                if (!mbar_wait(&S.full_a[st], par, abort_flag, err)) break;
+            int g = 0, it = 0;
+            for (int work = blockIdx.x; work < n_work && !*abort_flag; work += gridDim.x, ++it) {
+                int e, t0, ntok;
+                decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+                const int nsub = (ntok + kSub - 1) / kSub;
+                uint32_t id0 = idesc_bf16(128, min(kSub, ntok));
+                int n1 = ntok - kSub, n2 = ntok - 2 * kSub;
+                uint32_t id1 = idesc_bf16(128, n1 <= 0 ? 16 : (min(kSub, n1) + 15) & ~15);
+                uint32_t id2 = idesc_bf16(128, n2 <= 0 ? 16 : (min(kSub, n2) + 15) & ~15);
+                id0 = idesc_bf16(128, (min(kSub, ntok) + 15) & ~15);
+                // the epilogue of the previous tile must have drained the accumulators
+                if (!mbar_wait(&S.acc_empty, (it & 1) ^ 1, abort_flag, err)) break;
                 tc_fence_after();
-                uint32_t bst = smem_u32(sbase + (size_t)st * kStageBytes);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int st = g % kStages;
+                    const uint32_t par = (g / kStages) & 1;
+                    if (!mbar_wait(&S.full_b[st], par, abort_flag, err)) break;
+                    if (!mbar_wait(&S.full_a[st], par, abort_flag, err)) break;
+                    tc_fence_after();
+                    const uint32_t bst = smem_u32(sbase + (size_t)st * kStageBytes);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    uint32_t a_t = tbase + kAcol + st * 32 + kk * 8;
-                    for (int j = 0; j < nsub; ++j) {
-                        uint64_t bd = smem_desc_sw128(bst + j * kSubBytes + kk * 32);
-                        mma_ts(tbase + j * kSub, a_t, bd, idesc[j], (kb | kk) != 0);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint32_t a_t = tbase + kAcol + st * 32 + kk * 8;
+                        const uint32_t acc = (kb | kk) != 0;
+                        mma_ts(tbase, a_t, smem_desc_sw128(bst + kk * 32), id0, acc);
+                        if (nsub > 1) mma_ts(tbase + kSub, a_t, smem_desc_sw128(bst + kSubBytes + kk * 32), id1, acc);
+                        if (nsub > 2) mma_ts(tbase + 2 * kSub, a_t, smem_desc_sw128(bst + 2 * kSubBytes + kk * 32), id2, acc);
                     }
+                    mma_commit(&S.empty[st]);
                 }
-                mma_commit(&S.empty[st]);
+                mma_commit(&S.acc);
             }
-            mma_commit(&S.acc);
         }
     } else if (warp >= 4) {
-        // ---------------- dequant producers, then epilogue ----------------
-        const int t = tid - 128;                 // TMEM lane = weight row of this tile
-        const uint32_t lane_base = (uint32_t)(warp & 3) * 32;
-        int row_st;                              // storage row inside the expert
-        int j0 = 0, h0 = 0;
+        // ---------------- dequant producers + epilogue ----------------
+        const int t = tid - 128;  // TMEM lane = weight row of the tile
+        const uint32_t lane_off = ((uint32_t)(warp & 3) * 32) << 16;
         const int I = R / 2;
-        if (MODE == MODE_GATE_UP) {
-            j0 = blockIdx.x * 64;
-            row_st = t < 64 ? j0 + t : I + j0 + (t - 64);
-        } else {
-            h0 = blockIdx.x * 128;
-            row_st = h0 + t;
-        }
-        const int64_t grow = (int64_t)e * R + row_st;
-        const uint4 *qrow = reinterpret_cast<const uint4 *>(w.q + grow * (K / 2));
-        const int64_t gbase = grow * (int64_t)K;
-        const uint16_t *sz_s = w.s, *sz_z = w.z;
         const int gs = w.group_size;
-        // overlay cursor of this row (CSR sorted by column)
-        int cur = 0, cend = 0, ncol = 0x7fffffff;
-        float nval = 0.0f;
-        if (w.n_ov > 0) {
-            cur = w.row_ptr[grow];
-            cend = w.row_ptr[grow + 1];
-            if (cur < cend) { ncol = w.col[cur]; nval = w.val[cur]; }
-        }
-        uint4 qa[4], qb[4];
-        uint16_t ss[4], zz[4];
-        auto load = [&](int kb, uint4 &a, uint4 &b, uint16_t &s_, uint16_t &z_) {
-            a = __ldg(qrow + kb * 2);
-            b = __ldg(qrow + kb * 2 + 1);
-            int64_t g = (gbase + (int64_t)kb * kBK) / gs;
-            s_ = __ldg(sz_s + g);
-            z_ = __ldg(sz_z + g);
-        };
-#pragma unroll
-        for (int d = 0; d < 3; ++d)
-            if (d < nk) load(d, qa[d], qb[d], ss[d], zz[d]);
+        const unsigned short *s_ptr = reinterpret_cast<const unsigned short *>(w.s);
+        const unsigned short *z_ptr = reinterpret_cast<const unsigned short *>(w.z);
+        int g = 0, it = 0;
         bool ok = true;
-        for (int kb0 = 0; kb0 < nk && ok; kb0 += 4) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int kb = kb0 + u;
-                if (kb < nk && ok) {
-                    if (kb + 3 < nk) load(kb + 3, qa[(u + 3) & 3], qb[(u + 3) & 3], ss[(u + 3) & 3], zz[(u + 3) & 3]);
-                    const int st = kb % kStages;
-                    const uint32_t par = ((kb / kStages) & 1) ^ 1;
-                    uint32_t r[32];
-                    dequant_block(qa[u], qb[u], ss[u], zz[u], r);
-                    const int k0 = kb * kBK;
-                    while (ncol < k0 + kBK) {
-                        const int c = ncol - k0;
-                        const uint32_t vb = __bfloat16_as_ushort(__float2bfloat16_rn(nval));
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (i == (c >> 1))
-                                r[i] = (c & 1) ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
+        for (int work = blockIdx.x; work < n_work && ok; work += gridDim.x, ++it) {
+            int e, t0, ntok;
+            decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+            const int rb = work % nrb;
+            const int row0 = pl.expert_off[e] + t0;
+            int row_st, j0 = 0, h0 = 0;
+            if (MODE == MODE_GATE_UP) {
+                j0 = rb * 64;
+                row_st = t < 64 ? j0 + t : I + j0 + (t - 64);
+            } else {
+                h0 = rb * 128;
+                row_st = h0 + t;
+            }
+            const int64_t grow = (int64_t)e * R + row_st;
+            const uint4 *qrow = reinterpret_cast<const uint4 *>(w.q + grow * (K / 2));
+            const int64_t gbase = grow * (int64_t)K;
+            int cur = 0, cend = 0, ncol = 0x7fffffff;
+            float nval = 0.0f;
+            if (w.n_ov > 0) {
+                cur = w.row_ptr[grow];
+                cend = w.row_ptr[grow + 1];
+                if (cur < cend) { ncol = w.col[cur]; nval = w.val[cur]; }
+            }
+            // rolling 3-deep prefetch ring of (codes, scale|zero)
+            uint4 a0 = make_uint4(0, 0, 0, 0), b0 = a0, a1 = a0, b1 = a0, a2 = a0, b2 = a0;
+            uint32_t z0 = 0, z1 = 0, z2 = 0;
+#define USAF_LOAD(kb_, A_, B_, Z_)                                                           \
+    do {                                                                                     \
+        A_ = __ldg(qrow + (kb_) * 2);                                                        \
+        B_ = __ldg(qrow + (kb_) * 2 + 1);                                                    \
+        int64_t gg = (gbase + (int64_t)(kb_) * kBK) / gs;                                    \
+        Z_ = (uint32_t)__ldg(s_ptr + gg) | ((uint32_t)__ldg(z_ptr + gg) << 16);              \
+    } while (0)
+            USAF_LOAD(0, a0, b0, z0);
+            if (1 < nk) USAF_LOAD(1, a1, b1, z1);
+            if (2 < nk) USAF_LOAD(2, a2, b2, z2);
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                uint4 na = a2, nb = b2;
+                uint32_t nz = z2;
+                if (kb + 3 < nk) USAF_LOAD(kb + 3, na, nb, nz);
+                uint32_t r[32];
+                dequant_block(a0, b0, (uint16_t)(z0 & 0xFFFF), (uint16_t)(z0 >> 16), r);
+                const int k0 = kb * kBK;
+                if (ncol < k0 + kBK) {
+                    // trained coordinates of this row in this k-block (rare): patch
+                    do {
+                        patch_elem(r, ncol - k0, __bfloat16_as_ushort(__float2bfloat16_rn(nval)));
                         ++cur;
                         if (cur < cend) { ncol = w.col[cur]; nval = w.val[cur]; }
                         else ncol = 0x7fffffff;
-                    }
-                    if (!mbar_wait(&S.empty[st], par, abort_flag, err)) { ok = false; break; }
-                    tc_fence_after();
-                    tmem_st_32x32b_x32(tbase + (lane_base << 16) + kAcol + st * 32, r);
-                    tmem_wait_st();
-                    tc_fence_before();
-                    mbar_arrive(&S.full_a[st]);
+                    } while (ncol < k0 + kBK);
                 }
+                const int st = g % kStages;
+                if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
+                tc_fence_after();
+                tmem_st_32x32b_x32(tbase + lane_off + kAcol + st * 32, r);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&S.full_a[st]);
+                a0 = a1; b0 = b1; z0 = z1;
+                a1 = a2; b1 = b2; z1 = z2;
+                a2 = na; b2 = nb; z2 = nz;
             }
-        }
-        // ---- epilogue ----
-        drain_wait(&S.acc, 0, err);
-        tc_fence_after();
-        fence_proxy_async();
-        __nv_bfloat16 *stg = reinterpret_cast<__nv_bfloat16 *>(sbase);  // [32 tokens][kStageLd]
-        if (!*abort_flag) {
+#undef USAF_LOAD
+            if (!ok) break;
+            // ---- epilogue of this tile ----
+            if (!mbar_wait(&S.acc, it & 1, abort_flag, err)) { ok = false; break; }
+            tc_fence_after();
+            fence_proxy_async();
             for (int c0 = 0; c0 < ntok; c0 += 32) {
                 uint32_t v[32];
-                tmem_ld_32x32b_x32(tbase + (lane_base << 16) + c0, v);
+                tmem_ld_32x32b_x32(tbase + lane_off + c0, v);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
@@ -279,8 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int j = item >> 4, sg = item & 15;
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
-                            uint4 val = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
-                            *reinterpret_cast<uint4 *>(out0 + slot * R + h0 + sg * 8) = val;
+                            *reinterpret_cast<uint4 *>(out0 + slot * R + h0 + sg * 8) =
+                                *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
                         }
                     }
                 } else {
@@ -295,10 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __align__(16) __nv_bfloat16 h8[8];
 #pragma unroll
                             for (int q = 0; q < 8; ++q) {
-                                float g = __bfloat162float(g8[q]);
-                                float sg_ = __bfloat162float(__float2bfloat16_rn(
-                                    __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
-                                h8[q] = __float2bfloat16_rn(__fmul_rn(sg_, __bfloat162float(u8[q])));
+                                float gf = __bfloat162float(g8[q]);
+                                float sf = __bfloat162float(__float2bfloat16_rn(
+                                    __fdiv_rn(gf, __fadd_rn(1.0f, expf(-gf)))));
+                                h8[q] = __float2bfloat16_rn(__fmul_rn(sf, __bfloat162float(u8[q])));
                             }
                             *reinterpret_cast<uint4 *>(out0 + slot * R + j0 + sg * 8) = gv;
                             *reinterpret_cast<uint4 *>(out0 + slot * R + I + j0 + sg * 8) = uv;
@@ -309,7 +377,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 named_bar_sync(1, 128);
             }
+            tc_fence_before();
+            mbar_arrive(&S.acc_empty);
         }
+        if (!ok) drain_wait(&S.acc, it & 1, err);  // MMAs of an aborted tile finish before dealloc
         tc_fence_before();
     }
     __syncthreads();
@@ -360,15 +431,21 @@ int launch_fwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bflo
         attr_set = true;
     }
     int nrb = MODE == MODE_GATE_UP ? (w->R / 2) / 64 : w->R / 128;
-    int tiles = pl->P_cap / kMaxTok + 1 + pl->E;
-    dim3 grid(nrb, tiles);
-    tc_fwd_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(tm, *pl, *w, out0, out1);
+    int sms = 148;
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    int work_ub = (pl->P_cap / kMaxTok + 1 + pl->E) * nrb;
+    dim3 grid(std::min(sms, work_ub));
+    tc_fwd_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(tm, *pl, *w, out0, out1, nrb);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
 
 bool shape_ok_common(const usaf_qweight *w) {
-    return w->C % kBK == 0 && w->group_size % kBK == 0 && w->C % 32 == 0 &&
+    return w->E <= 1024 && w->C % kBK == 0 && w->group_size % kBK == 0 && w->C % 32 == 0 &&
            encode_fn() != nullptr;
 }
 

@@ -46,26 +46,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes (or ~1 us passes) instead of spinning on the issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: ~2 s of wall clock, then flag the error and the CTA-wide
 // abort word so every role stops issuing new work.
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 
+__device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity,
+                                            volatile int *abort_flag, int *err) {
+    uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > kWaitBudgetNs) {
+            *abort_flag = 1;
+            atomicOr(err, USAF_ERR_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                           int *err) {
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = globaltimer();
-    uint32_t n = 0;
-    while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((++n & 63) == 0) {
-            if (*abort_flag) return false;
-            if (globaltimer() - t0 > kWaitBudgetNs) {
-                *abort_flag = 1;
-                atomicOr(err, USAF_ERR_WAIT_TIMEOUT);
-                return false;
-            }
-        }
-    }
+    return mbar_wait_slow(bar, parity, abort_flag, err);
 }
 
 __device__ __forceinline__ void fence_barrier_init() {
