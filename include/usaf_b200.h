@@ -77,6 +77,11 @@ typedef struct {
     const int32_t *colT_ptr;  /* [E*C+1]  CSC offsets                              */
     const int32_t *rowT;      /* [n_ov]   row of each CSC entry                    */
     const float   *valT;      /* [n_ov]   effective value of each CSC entry        */
+    /* optional column-major copy for the backward GEMMs (usaf_int4_transpose):
+     * qT [E*C*R/2] codes of storage column c packed along rows, and
+     * szT [E*(C/group_size)*R] uint32 (scale | zero << 16) per (column group, row) */
+    const int8_t   *qT;
+    const uint32_t *szT;
 } usaf_qweight;
 
 /* ---- int4 format ---------------------------------------------------------
@@ -89,6 +94,12 @@ int usaf_dequant_int4(const void *q, const void *s, const void *z, int64_t numel
                       int32_t group_size, int32_t out_dtype, void *out, void *stream);
 int usaf_quant_int4(const void *x, int32_t x_dtype, int64_t numel, int32_t group_size,
                     void *q, void *s, void *z, void *stream);
+
+/* usaf_int4_transpose: build the column-major copy (qT, szT) of a projection
+ * [E, R, C] for the tensor-core backward GEMMs.  Same codes, scales and
+ * zeros, re-laid so a storage column's codes are contiguous. */
+int usaf_int4_transpose(const void *q, const void *s, const void *z, int32_t E, int32_t R,
+                        int32_t C, int32_t group_size, void *qT, void *szT, void *stream);
 
 /* ---- router ----------------------------------------------------------------
  * usaf_router_fwd replaces the router of dml_qwen3_moe_block_forward

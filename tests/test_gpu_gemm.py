@@ -113,3 +113,32 @@ def test_grouped_gemms_vs_torch(dev, case):
     check(blk.y_seg[:P], y_ref, "down")
     if "zipf" in case:
         assert max(cnt) > 384
+
+    # backward: dh = dcur @ W_dn[e] with SwiGLU backward fused; dx = dgu @ W_gu[e]
+    H = case["H"]
+    g2 = torch.Generator(device=dev).manual_seed(7)
+    blk.dcur[:P] = torch.randn(P, H, device=dev, generator=g2).to(torch.bfloat16)
+    _lib.call("usaf_expert_down_bwd", blk.plan, p["down_proj"].struct(), _lib.ptr(blk.dcur),
+              _lib.ptr(blk.gu), _lib.BF16, _lib.ptr(blk.dgu), st)
+    _lib.call("usaf_expert_gate_up_bwd", blk.plan, p["gate_up_proj"].struct(), _lib.ptr(blk.dgu),
+              _lib.BF16, _lib.ptr(blk.dx_seg), st)
+    torch.cuda.synchronize()
+    blk.check()
+    dh_ref = torch.empty(P, I, device=dev)
+    for e in range(case["E"]):
+        if cnt[e]:
+            sl = slice(off[e], off[e] + cnt[e])
+            dh_ref[sl] = (blk.dcur[sl].float() @ wdn[e]).to(torch.bfloat16).float()
+    sg = (g / (1 + torch.exp(-g))).to(torch.bfloat16).float()
+    ds = (dh_ref * u).to(torch.bfloat16).float()
+    du_ref = (dh_ref * sg).to(torch.bfloat16).float()
+    sig = 1 / (1 + torch.exp(-g))
+    dg_ref = (ds * sig * (1 + g * (1 - sig))).to(torch.bfloat16).float()
+    check(blk.dgu[:P, I:], du_ref, "down_bwd/du")
+    check(blk.dgu[:P, :I], dg_ref, "down_bwd/dg")
+    dx_ref = torch.empty(P, H, device=dev)
+    for e in range(case["E"]):
+        if cnt[e]:
+            sl = slice(off[e], off[e] + cnt[e])
+            dx_ref[sl] = (blk.dgu[sl].float() @ wgu[e]).to(torch.bfloat16).float()
+    check(blk.dx_seg[:P], dx_ref, "gate_up_bwd")

@@ -40,7 +40,9 @@ constexpr int kAcol = kMaxTok;                   // first TMEM column of the A s
 constexpr int kThreads = 256;
 constexpr int kStageLd = 136;                    // epilogue staging row stride (elements)
 
-enum : int { MODE_GATE_UP = 0, MODE_DOWN = 1 };
+enum : int { MODE_GATE_UP = 0, MODE_DOWN = 1, MODE_DOWN_BWD = 2, MODE_GU_BWD = 3 };
+constexpr int kBoxRows = 32;                     // token rows per TMA box
+constexpr int kBoxBytes = kBoxRows * kBK * 2;    // 4 KB
 
 struct alignas(8) TcShared {
     uint64_t full_b[kStages];
@@ -53,9 +55,10 @@ struct alignas(8) TcShared {
 };
 
 constexpr size_t kStgBytes = (size_t)32 * kStageLd * 2;  // epilogue staging tile
-// stages + epilogue staging + shared block + per-expert tile prefix / counts (E <= 1024)
+constexpr size_t kSzBytes = (size_t)4 * kBK * 4;          // transposed-mode scale ring
+// stages + epilogue staging + scale ring + shared block + tile prefix / counts (E <= 1024)
 constexpr size_t kSmemBytes =
-    (size_t)kStages * kStageBytes + kStgBytes + sizeof(TcShared) + 8 * 1025 + 1024;
+    (size_t)kStages * kStageBytes + kStgBytes + kSzBytes + sizeof(TcShared) + 8 * 1025 + 1024;
 
 // time-bounded wait that ignores the abort flag (used to drain in-flight work)
 __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, int *err) {
@@ -86,13 +89,45 @@ __device__ __forceinline__ void dequant_block(uint4 a, uint4 b, uint16_t s_bits,
     }
 }
 
+// Replace element c (0..63) of a packed bf16x2 block with the bf16 bits vb.
+// A predicated select per register keeps r[] in registers (an indexed write
+// would move the whole block to local memory).
+__device__ __forceinline__ void patch_elem(uint32_t (&r)[32], int c, uint32_t vb) {
+    const uint32_t pi = (uint32_t)c >> 1;
+    const bool hi = c & 1;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t cand = hi ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
+        asm volatile("{\n .reg .pred p;\n setp.eq.u32 p, %1, %2;\n selp.b32 %0, %3, %0, p;\n}\n"
+                     : "+r"(r[i])
+                     : "r"(pi), "r"((uint32_t)i), "r"(cand));
+    }
+}
+
+// transposed-mode dequant: element pair j covers storage rows 2j, 2j+1 of one
+// column, each row with its own (scale, zero) from the staged scale block
+__device__ __forceinline__ void dequant_block_rows(uint4 a, uint4 b, const uint32_t *sz,
+                                                   uint32_t (&r)[32]) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const __half2 magic = __half2half2(__ushort_as_half((unsigned short)0x6400));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        uint32_t byte = (w[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+        uint32_t u = (byte & 0xFu) | ((byte & 0xF0u) << 12) | 0x64006400u;
+        __half2 c = __hsub2(*reinterpret_cast<__half2 *>(&u), magic);
+        uint32_t wa = sz[2 * j], wb = sz[2 * j + 1];
+        uint32_t s2u = __byte_perm(wa, wb, 0x5410), z2u = __byte_perm(wa, wb, 0x7632);
+        __half2 v = __hadd2_rn(__hmul2_rn(c, *reinterpret_cast<__half2 *>(&s2u)),
+                               *reinterpret_cast<__half2 *>(&z2u));
+        float2 f = __half22float2(v);
+        __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
+        r[j] = *reinterpret_cast<uint32_t *>(&bb);
+    }
+}
+
 // Work item = (token tile, row block); tile t of expert e covers tokens
 // [t0, t0+ntok) of e's segment.  Consecutive work items share a token tile
 // so its rows are reused from L2 across row blocks.
-struct TileMap {
-    int n_tiles;
-};
-
 __device__ __forceinline__ void decode_tile(const int *tile_off, const int *cnts, int E, int tile,
                                             int &e, int &t0, int &ntok) {
     int lo = 0, hi = E;  // first expert with tile_off[e+1] > tile
@@ -110,35 +145,30 @@ __device__ __forceinline__ void decode_tile(const int *tile_off, const int *cnts
     ntok = min(per, cnt - t0);
 }
 
-// Replace element c (0..63) of a packed bf16x2 block with the bf16 bits vb.
-// A predicated select per register keeps r[] in registers (an indexed write
-// would move the whole block to local memory).
-__device__ __forceinline__ void patch_elem(uint32_t (&r)[32], int c, uint32_t vb) {
-    const uint32_t pi = (uint32_t)c >> 1;
-    const bool hi = c & 1;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const uint32_t cand = hi ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
-        asm volatile("{\n .reg .pred p;\n setp.eq.u32 p, %1, %2;\n selp.b32 %0, %3, %0, p;\n}\n"
-                     : "+r"(r[i])
-                     : "r"(pi), "r"((uint32_t)i), "r"(cand));
-    }
-}
-
+// MODE_GATE_UP : rows = 64 gate + 64 up storage rows, K = C, SwiGLU epilogue
+//                (out0 = gu [P,R], out1 = h [P,R/2])
+// MODE_DOWN    : rows = 128 storage rows, K = C           (out0 = y [P,R])
+// MODE_DOWN_BWD: rows = 128 storage columns (W^T), K = R, SwiGLU backward
+//                epilogue (in1 = gu [P,2C], out0 = dgu [P,2C])
+// MODE_GU_BWD  : rows = 128 storage columns (W^T), K = R  (out0 = dx [P,C])
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_fwd_kernel(const __grid_constant__ CUtensorMap tmap_b, usaf_route_plan pl, usaf_qweight w,
-                  __nv_bfloat16 *__restrict__ out0, __nv_bfloat16 *__restrict__ out1, int nrb) {
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_b, usaf_route_plan pl, usaf_qweight w,
+                   __nv_bfloat16 *__restrict__ out0, __nv_bfloat16 *__restrict__ out1,
+                   const __nv_bfloat16 *__restrict__ in1, int nrb) {
+    constexpr bool TRANS = MODE >= MODE_DOWN_BWD;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *sbase = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     __nv_bfloat16 *stg = reinterpret_cast<__nv_bfloat16 *>(sbase + (size_t)kStages * kStageBytes);
-    TcShared &S = *reinterpret_cast<TcShared *>(sbase + (size_t)kStages * kStageBytes + kStgBytes);
+    uint32_t *sz_ring = reinterpret_cast<uint32_t *>(sbase + (size_t)kStages * kStageBytes + kStgBytes);
+    TcShared &S = *reinterpret_cast<TcShared *>(sbase + (size_t)kStages * kStageBytes + kStgBytes + kSzBytes);
     int *tile_off = reinterpret_cast<int *>(&S + 1);         // [E+1]
     int *cnts = tile_off + (pl.E + 1);                        // [E]
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int K = w.C, R = w.R, E = pl.E;
+    const int R = w.R, C = w.C, E = pl.E;
+    const int K = TRANS ? R : C;
     const int nk = K / kBK;
     int *err = pl.err;
 
@@ -194,23 +224,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tbase = S.tmem_base;
 
     if (warp == 0) {
-        // ---------------- TMA producer (tokens) ----------------
+        // ---------------- TMA producer (token rows, 32-row boxes) ----------------
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
-            int g = 0;  // global k-block counter (shared sequence with the other roles)
-            int last_g = -1;  // last issued k-block; stages of the final kStages are in flight
+            int g = 0, last_g = -1;
             for (int work = blockIdx.x; work < n_work && !*abort_flag; work += gridDim.x) {
                 int e, t0, ntok;
                 decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
                 const int row0 = pl.expert_off[e] + t0;
-                const int nsub = (ntok + kSub - 1) / kSub;
+                const int nbox = (ntok + kBoxRows - 1) / kBoxRows;
+                const int rb = work % nrb;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int st = g % kStages;
                     if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) break;
-                    mbar_arrive_expect_tx(&S.full_b[st], (uint32_t)(nsub * kSubBytes));
+                    mbar_arrive_expect_tx(&S.full_b[st], (uint32_t)(nbox * kBoxBytes + (TRANS ? kBK * 4 : 0)));
                     unsigned char *dst = sbase + (size_t)st * kStageBytes;
-                    for (int j = 0; j < nsub; ++j)
-                        tma_load_2d(dst + j * kSubBytes, &tmap_b, &S.full_b[st], kb * kBK, row0 + j * kSub);
+                    for (int j = 0; j < nbox; ++j)
+                        tma_load_2d(dst + j * kBoxBytes, &tmap_b, &S.full_b[st], kb * kBK, row0 + j * kBoxRows);
+                    if (TRANS) {
+                        // per-row (scale|zero) words of this k-block for the column group
+                        const uint32_t *src = w.szT + ((int64_t)e * (C / w.group_size) +
+                                                       (rb * 128) / w.group_size) * R + kb * kBK;
+                        bulk_load(sz_ring + st * kBK, src, kBK * 4, &S.full_b[st]);
+                    }
                     last_g = g;
                 }
             }
@@ -227,11 +263,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int e, t0, ntok;
                 decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
                 const int nsub = (ntok + kSub - 1) / kSub;
-                uint32_t id0 = idesc_bf16(128, min(kSub, ntok));
-                int n1 = ntok - kSub, n2 = ntok - 2 * kSub;
-                uint32_t id1 = idesc_bf16(128, n1 <= 0 ? 16 : (min(kSub, n1) + 15) & ~15);
-                uint32_t id2 = idesc_bf16(128, n2 <= 0 ? 16 : (min(kSub, n2) + 15) & ~15);
-                id0 = idesc_bf16(128, (min(kSub, ntok) + 15) & ~15);
+                const int n0 = min(kSub, ntok), n1 = ntok - kSub, n2 = ntok - 2 * kSub;
+                const uint32_t id0 = idesc_bf16(128, (n0 + 15) & ~15);
+                const uint32_t id1 = idesc_bf16(128, n1 <= 0 ? 16 : (min(kSub, n1) + 15) & ~15);
+                const uint32_t id2 = idesc_bf16(128, n2 <= 0 ? 16 : (min(kSub, n2) + 15) & ~15);
                 // the epilogue of the previous tile must have drained the accumulators
                 if (!mbar_wait(&S.acc_empty, (it & 1) ^ 1, abort_flag, err)) break;
                 tc_fence_after();
@@ -257,9 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         // ---------------- dequant producers + epilogue ----------------
-        const int t = tid - 128;  // TMEM lane = weight row of the tile
+        const int t = tid - 128;  // TMEM lane
         const uint32_t lane_off = ((uint32_t)(warp & 3) * 32) << 16;
-        const int I = R / 2;
         const int gs = w.group_size;
         const unsigned short *s_ptr = reinterpret_cast<const unsigned short *>(w.s);
         const unsigned short *z_ptr = reinterpret_cast<const unsigned short *>(w.z);
@@ -270,33 +304,43 @@ __global__ void __launch_bounds__(kThreads, 1)
             decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
             const int rb = work % nrb;
             const int row0 = pl.expert_off[e] + t0;
-            int row_st, j0 = 0, h0 = 0;
+            // code row of this lane, and where its output lives
+            int64_t crow;        // row index into q (fwd) or qT (bwd)
+            int j0 = 0, h0 = 0;  // output column base
             if (MODE == MODE_GATE_UP) {
+                const int I = R / 2;
                 j0 = rb * 64;
-                row_st = t < 64 ? j0 + t : I + j0 + (t - 64);
-            } else {
+                crow = (int64_t)e * R + (t < 64 ? j0 + t : I + j0 + (t - 64));
+            } else if (MODE == MODE_DOWN) {
                 h0 = rb * 128;
-                row_st = h0 + t;
+                crow = (int64_t)e * R + h0 + t;
+            } else {
+                h0 = rb * 128;   // storage column block
+                crow = (int64_t)e * C + h0 + t;
             }
-            const int64_t grow = (int64_t)e * R + row_st;
-            const uint4 *qrow = reinterpret_cast<const uint4 *>(w.q + grow * (K / 2));
-            const int64_t gbase = grow * (int64_t)K;
+            const uint4 *qrow = reinterpret_cast<const uint4 *>((TRANS ? w.qT : w.q) + crow * (K / 2));
+            const int64_t gbase = crow * (int64_t)K;
             int cur = 0, cend = 0, ncol = 0x7fffffff;
             float nval = 0.0f;
+            const int32_t *ov_ptr = TRANS ? w.colT_ptr : w.row_ptr;
+            const int32_t *ov_idx = TRANS ? w.rowT : w.col;
+            const float *ov_val = TRANS ? w.valT : w.val;
             if (w.n_ov > 0) {
-                cur = w.row_ptr[grow];
-                cend = w.row_ptr[grow + 1];
-                if (cur < cend) { ncol = w.col[cur]; nval = w.val[cur]; }
+                cur = ov_ptr[crow];
+                cend = ov_ptr[crow + 1];
+                if (cur < cend) { ncol = ov_idx[cur]; nval = ov_val[cur]; }
             }
             // rolling 3-deep prefetch ring of (codes, scale|zero)
             uint4 a0 = make_uint4(0, 0, 0, 0), b0 = a0, a1 = a0, b1 = a0, a2 = a0, b2 = a0;
             uint32_t z0 = 0, z1 = 0, z2 = 0;
-#define USAF_LOAD(kb_, A_, B_, Z_)                                                           \
-    do {                                                                                     \
-        A_ = __ldg(qrow + (kb_) * 2);                                                        \
-        B_ = __ldg(qrow + (kb_) * 2 + 1);                                                    \
-        int64_t gg = (gbase + (int64_t)(kb_) * kBK) / gs;                                    \
-        Z_ = (uint32_t)__ldg(s_ptr + gg) | ((uint32_t)__ldg(z_ptr + gg) << 16);              \
+#define USAF_LOAD(kb_, A_, B_, Z_)                                                               \
+    do {                                                                                         \
+        A_ = __ldg(qrow + (kb_) * 2);                                                            \
+        B_ = __ldg(qrow + (kb_) * 2 + 1);                                                        \
+        if (!TRANS) {                                                                            \
+            int64_t gg = (gbase + (int64_t)(kb_) * kBK) / gs;                                    \
+            Z_ = (uint32_t)__ldg(s_ptr + gg) | ((uint32_t)__ldg(z_ptr + gg) << 16);              \
+        }                                                                                        \
     } while (0)
             USAF_LOAD(0, a0, b0, z0);
             if (1 < nk) USAF_LOAD(1, a1, b1, z1);
@@ -306,18 +350,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t nz = z2;
                 if (kb + 3 < nk) USAF_LOAD(kb + 3, na, nb, nz);
                 uint32_t r[32];
-                dequant_block(a0, b0, (uint16_t)(z0 & 0xFFFF), (uint16_t)(z0 >> 16), r);
+                const int st = g % kStages;
+                if (TRANS) {
+                    // this k-block's 64 per-row (scale|zero) words arrive with the stage's TMA
+                    if (!mbar_wait(&S.full_b[st], (g / kStages) & 1, abort_flag, err)) { ok = false; break; }
+                    const uint32_t *ring = sz_ring + st * kBK;
+                    uint32_t szr[kBK];
+#pragma unroll
+                    for (int i = 0; i < kBK / 4; ++i) {
+                        uint4 v4 = *reinterpret_cast<const uint4 *>(ring + 4 * i);
+                        szr[4 * i] = v4.x; szr[4 * i + 1] = v4.y; szr[4 * i + 2] = v4.z; szr[4 * i + 3] = v4.w;
+                    }
+                    dequant_block_rows(a0, b0, szr, r);
+                } else {
+                    dequant_block(a0, b0, (uint16_t)(z0 & 0xFFFF), (uint16_t)(z0 >> 16), r);
+                }
                 const int k0 = kb * kBK;
                 if (ncol < k0 + kBK) {
-                    // trained coordinates of this row in this k-block (rare): patch
+                    // trained coordinates of this lane in this k-block (rare): patch
                     do {
                         patch_elem(r, ncol - k0, __bfloat16_as_ushort(__float2bfloat16_rn(nval)));
                         ++cur;
-                        if (cur < cend) { ncol = w.col[cur]; nval = w.val[cur]; }
+                        if (cur < cend) { ncol = ov_idx[cur]; nval = ov_val[cur]; }
                         else ncol = 0x7fffffff;
                     } while (ncol < k0 + kBK);
                 }
-                const int st = g % kStages;
                 if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
                 tc_fence_after();
                 tmem_st_32x32b_x32(tbase + lane_off + kAcol + st * 32, r);
@@ -333,7 +390,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ---- epilogue of this tile ----
             if (!mbar_wait(&S.acc, it & 1, abort_flag, err)) { ok = false; break; }
             tc_fence_after();
-            fence_proxy_async();
             for (int c0 = 0; c0 < ntok; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + lane_off + c0, v);
@@ -342,16 +398,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int i = 0; i < 32; ++i)
                     stg[i * kStageLd + t] = __float2bfloat16_rn(__uint_as_float(v[i]));
                 named_bar_sync(1, 128);
-                if (MODE == MODE_DOWN) {
+                if (MODE == MODE_DOWN || MODE == MODE_GU_BWD) {
+                    const int ld = MODE == MODE_DOWN ? R : C;
                     for (int item = t; item < 32 * 16; item += 128) {
                         const int j = item >> 4, sg = item & 15;
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
-                            *reinterpret_cast<uint4 *>(out0 + slot * R + h0 + sg * 8) =
+                            *reinterpret_cast<uint4 *>(out0 + slot * ld + h0 + sg * 8) =
                                 *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
                         }
                     }
-                } else {
+                } else if (MODE == MODE_GATE_UP) {
+                    const int I = R / 2;
                     for (int item = t; item < 32 * 8; item += 128) {
                         const int j = item >> 3, sg = item & 7;
                         if (c0 + j < ntok) {
@@ -372,6 +430,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                             *reinterpret_cast<uint4 *>(out0 + slot * R + I + j0 + sg * 8) = uv;
                             *reinterpret_cast<uint4 *>(out1 + slot * I + j0 + sg * 8) =
                                 *reinterpret_cast<const uint4 *>(h8);
+                        }
+                    }
+                } else {  // MODE_DOWN_BWD: SwiGLU backward with the forward's gate/up
+                    const int I = C;
+                    for (int item = t; item < 32 * 16; item += 128) {
+                        const int j = item >> 4, sg = item & 15;
+                        if (c0 + j < ntok) {
+                            const int64_t slot = row0 + c0 + j;
+                            const int i0 = h0 + sg * 8;
+                            uint4 dv = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
+                            uint4 gv = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * I + i0);
+                            uint4 uv = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * I + I + i0);
+                            const __nv_bfloat16 *d8 = reinterpret_cast<const __nv_bfloat16 *>(&dv);
+                            const __nv_bfloat16 *g8 = reinterpret_cast<const __nv_bfloat16 *>(&gv);
+                            const __nv_bfloat16 *u8 = reinterpret_cast<const __nv_bfloat16 *>(&uv);
+                            __align__(16) __nv_bfloat16 dg8[8], du8[8];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                float dh = __bfloat162float(d8[q]);
+                                float gf = __bfloat162float(g8[q]), uf = __bfloat162float(u8[q]);
+                                float sg_ = __bfloat162float(__float2bfloat16_rn(
+                                    __fdiv_rn(gf, __fadd_rn(1.0f, expf(-gf)))));
+                                float ds = __bfloat162float(__float2bfloat16_rn(__fmul_rn(dh, uf)));
+                                du8[q] = __float2bfloat16_rn(__fmul_rn(dh, sg_));
+                                float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gf)));
+                                float tt = __fadd_rn(1.0f, __fmul_rn(gf, __fsub_rn(1.0f, sig)));
+                                dg8[q] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(ds, sig), tt));
+                            }
+                            *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + i0) = *reinterpret_cast<const uint4 *>(dg8);
+                            *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + I + i0) = *reinterpret_cast<const uint4 *>(du8);
                         }
                     }
                 }
@@ -403,14 +491,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// row-major bf16 matrix [rows, cols] -> tiles of 128 rows x 64 cols, 128-byte swizzle
+// row-major bf16 matrix [rows, cols] -> boxes of 32 rows x 64 cols, 128-byte swizzle
 bool make_tmap_rows(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols) {
     auto fn = encode_fn();
     if (!fn) return false;
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (cols * 2) % 16) return false;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kSub};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBoxRows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides,
                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -418,59 +506,70 @@ bool make_tmap_rows(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols)
     return r == CUDA_SUCCESS;
 }
 
+int num_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
 template <int MODE>
-int launch_fwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *act,
-               __nv_bfloat16 *out0, __nv_bfloat16 *out1, cudaStream_t st) {
+int launch_tc(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *act,
+              __nv_bfloat16 *out0, __nv_bfloat16 *out1, const __nv_bfloat16 *in1, cudaStream_t st) {
+    constexpr bool TRANS = MODE >= MODE_DOWN_BWD;
+    const int K = TRANS ? w->R : w->C;
     CUtensorMap tm;
-    if (!make_tmap_rows(&tm, act, pl->P_cap, w->C)) return USAF_EUNSUPPORTED;
+    if (!make_tmap_rows(&tm, act, pl->P_cap, K)) return USAF_EUNSUPPORTED;
     static bool attr_set = false;
     if (!attr_set) {
-        if (cudaFuncSetAttribute(tc_fwd_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(tc_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kSmemBytes) != cudaSuccess)
             return USAF_ECUDA;
         attr_set = true;
     }
-    int nrb = MODE == MODE_GATE_UP ? (w->R / 2) / 64 : w->R / 128;
-    int sms = 148;
-    {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    }
+    int nrb = MODE == MODE_GATE_UP ? (w->R / 2) / 64 : (MODE == MODE_DOWN ? w->R / 128 : w->C / 128);
     int work_ub = (pl->P_cap / kMaxTok + 1 + pl->E) * nrb;
-    dim3 grid(std::min(sms, work_ub));
-    tc_fwd_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(tm, *pl, *w, out0, out1, nrb);
+    dim3 grid(std::min(num_sms(), work_ub));
+    tc_gemm_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(tm, *pl, *w, out0, out1, in1, nrb);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
 
 bool shape_ok_common(const usaf_qweight *w) {
-    return w->E <= 1024 && w->C % kBK == 0 && w->group_size % kBK == 0 && w->C % 32 == 0 &&
-           encode_fn() != nullptr;
+    return w->E <= 1024 && w->C % kBK == 0 && w->R % kBK == 0 && w->group_size % kBK == 0 &&
+           w->C % 32 == 0 && encode_fn() != nullptr;
 }
 
 }  // namespace
 
-bool tc_supported_gate_up(const usaf_qweight *w) { return shape_ok_common(w) && (w->R / 2) % 64 == 0 && w->R % 2 == 0; }
+bool tc_supported_gate_up(const usaf_qweight *w) { return shape_ok_common(w) && w->R % 128 == 0; }
 bool tc_supported_down(const usaf_qweight *w) { return shape_ok_common(w) && w->R % 128 == 0; }
-bool tc_supported_down_bwd(const usaf_qweight *) { return false; }
-bool tc_supported_gate_up_bwd(const usaf_qweight *) { return false; }
+static bool trans_ok(const usaf_qweight *w) {
+    return shape_ok_common(w) && w->qT && w->szT && w->C % 128 == 0 && w->group_size % 128 == 0 &&
+           (w->n_ov == 0 || (w->colT_ptr && w->rowT && w->valT));
+}
+bool tc_supported_down_bwd(const usaf_qweight *w) { return trans_ok(w); }
+bool tc_supported_gate_up_bwd(const usaf_qweight *w) { return trans_ok(w); }
 
 int tc_gate_up_fwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *x_perm,
                    __nv_bfloat16 *gu, __nv_bfloat16 *h, cudaStream_t st) {
-    return launch_fwd<MODE_GATE_UP>(pl, w, x_perm, gu, h, st);
+    return launch_tc<MODE_GATE_UP>(pl, w, x_perm, gu, h, nullptr, st);
 }
 int tc_down_fwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *h,
                 __nv_bfloat16 *y_seg, cudaStream_t st) {
-    return launch_fwd<MODE_DOWN>(pl, w, h, y_seg, nullptr, st);
+    return launch_tc<MODE_DOWN>(pl, w, h, y_seg, nullptr, nullptr, st);
 }
-int tc_down_bwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *,
-                const __nv_bfloat16 *, __nv_bfloat16 *, cudaStream_t) {
-    return USAF_EUNSUPPORTED;
+int tc_down_bwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *dcur,
+                const __nv_bfloat16 *gu, __nv_bfloat16 *dgu, cudaStream_t st) {
+    return launch_tc<MODE_DOWN_BWD>(pl, w, dcur, dgu, nullptr, gu, st);
 }
-int tc_gate_up_bwd(const usaf_route_plan *, const usaf_qweight *, const __nv_bfloat16 *,
-                   __nv_bfloat16 *, cudaStream_t) {
-    return USAF_EUNSUPPORTED;
+int tc_gate_up_bwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *dgu,
+                   __nv_bfloat16 *dx_seg, cudaStream_t st) {
+    return launch_tc<MODE_GU_BWD>(pl, w, dgu, dx_seg, nullptr, nullptr, st);
 }
 
 }  // namespace usaf

@@ -185,3 +185,49 @@ extern "C" int usaf_quant_int4(const void *x, int32_t x_dtype, int64_t numel, in
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
+
+// ---- column-major copy for the backward GEMMs ------------------------------
+namespace usaf {
+// qT[(e*C + c)*(R/2) + rp] = code(e, 2rp, c) | code(e, 2rp+1, c) << 4
+__global__ void int4_transpose_codes(const uint8_t *__restrict__ q, int E, int R, int C,
+                                     uint8_t *__restrict__ qT) {
+    const int64_t total = (int64_t)E * C * (R / 2);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t rp = i % (R / 2);
+        int64_t ec = i / (R / 2);
+        int64_t c = ec % C, e = ec / C;
+        int64_t f0 = ((e * R + 2 * rp) * C + c), f1 = f0 + C;
+        uint32_t c0 = (q[f0 >> 1] >> ((f0 & 1) * 4)) & 0xF;
+        uint32_t c1 = (q[f1 >> 1] >> ((f1 & 1) * 4)) & 0xF;
+        qT[i] = (uint8_t)(c0 | (c1 << 4));
+    }
+}
+// szT[(e*(C/gs) + cb)*R + r] = s[(e*R + r)*(C/gs) + cb] | z[...] << 16
+__global__ void int4_transpose_scales(const uint16_t *__restrict__ s, const uint16_t *__restrict__ z,
+                                      int E, int R, int C, int gs, uint32_t *__restrict__ szT) {
+    const int ncb = C / gs;
+    const int64_t total = (int64_t)E * ncb * R;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = i % R;
+        int64_t ecb = i / R;
+        int64_t cb = ecb % ncb, e = ecb / ncb;
+        int64_t src = (e * R + r) * ncb + cb;
+        szT[i] = (uint32_t)s[src] | ((uint32_t)z[src] << 16);
+    }
+}
+}  // namespace usaf
+
+extern "C" int usaf_int4_transpose(const void *q, const void *s, const void *z, int32_t E, int32_t R,
+                                   int32_t C, int32_t group_size, void *qT, void *szT, void *stream) {
+    USAF_REQUIRE(q && s && z && qT && szT && E >= 1 && R >= 2 && C >= 1 && group_size >= 1);
+    if (R % 2 || C % group_size) return USAF_EUNSUPPORTED;
+    cudaStream_t st = as_stream(stream);
+    unsigned grid = 148 * 16;
+    int4_transpose_codes<<<grid, 256, 0, st>>>((const uint8_t *)q, E, R, C, (uint8_t *)qT);
+    int4_transpose_scales<<<grid, 256, 0, st>>>((const uint16_t *)s, (const uint16_t *)z, E, R, C,
+                                                group_size, (uint32_t *)szT);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
+}

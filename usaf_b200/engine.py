@@ -106,6 +106,13 @@ class Projection:
         self.colT_ptr = self.rowT = self.valT = None
         self.csr_to_compact = self.compact_to_csr = self.compact_to_csc = None
         self.scratch = None
+        self.qT = self.szT = None
+        if dtype == torch.bfloat16 and R % 2 == 0:
+            # column-major copy for the tensor-core backward GEMMs (built once)
+            self.qT = torch.empty_like(self.q)
+            self.szT = torch.empty(E * (Cc // group_size) * R, dtype=torch.int32, device=self.device)
+            call("usaf_int4_transpose", ptr(self.q), ptr(self.s), ptr(self.z), E, R, Cc, group_size,
+                 ptr(self.qT), ptr(self.szT), stream())
         self._struct = None
 
     def numel(self) -> int:
@@ -158,6 +165,7 @@ class Projection:
             if self.n_ov:
                 st.row_ptr, st.col, st.val = ptr(self.row_ptr), ptr(self.col), ptr(self.val)
                 st.colT_ptr, st.rowT, st.valT = ptr(self.colT_ptr), ptr(self.rowT), ptr(self.valT)
+            st.qT, st.szT = ptr(self.qT), ptr(self.szT)
             self._struct = st
         return self._struct
 
