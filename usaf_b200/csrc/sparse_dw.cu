@@ -9,69 +9,152 @@
 //   g = dtype( sum over expert e's slots s of gout[s, r] * gin[s, c] )
 // in a fixed slot order (deterministic), then compact[pos] += scale * g.
 //
-// Work item = (expert, block of 256 storage rows); one thread per row walks
-// that row's CSR entries.  Token chunks of gin (all columns) and gout (the
-// block's rows) are staged transposed in shared memory so every coordinate
-// reads contiguous token runs; per-chunk partial sums go to an fp32 scratch
-// vector owned one-to-one by coordinates (no atomics).
+// Work item = (expert, block of 512 storage rows); each thread owns two rows
+// and walks their CSR entries.  Token chunks of gin (all columns) and gout
+// (the block's rows) are staged transposed in shared memory so every
+// coordinate reads contiguous token runs; per-chunk partial sums go to an
+// fp32 scratch vector owned one-to-one by coordinates (no atomics).
 #include "common.cuh"
 
 namespace usaf {
 
-constexpr int kRowsPerBlock = 256;
+constexpr int kRowsPerBlock = 512;   // storage rows per work item
+constexpr int kTC = 32;              // tokens per chunk
+constexpr int kThr = 256;
 
-template <typename Act, int TC>
-__global__ void __launch_bounds__(kRowsPerBlock) sddmm_kernel(
-    usaf_route_plan pl, usaf_qweight w, const Act *__restrict__ gout,
-    const Act *__restrict__ gin, const int32_t *__restrict__ csr_to_compact, float scale,
-    float *__restrict__ compact, float *__restrict__ scratch) {
+// Stage rows [t0, t0+tn) x columns [c0, c0+ncols) of a row-major [*, ld]
+// activation matrix transposed into dst[col][kTC] (token-contiguous rows of
+// 64 B for bf16 / 128 B for fp32).  16-byte chunks of each row are XOR
+// swizzled by the row index so the transposing stores spread over banks.
+template <typename Act>
+__device__ __forceinline__ void stage_transposed(const Act *__restrict__ src, int ld, int64_t row0,
+                                                 int tn, int c0, int ncols, Act *dst) {
+    constexpr int VEC = 16 / sizeof(Act);         // tokens per 16-byte chunk
+    constexpr int NCH = kTC / VEC;                // chunks per staged row
+    if (sizeof(Act) == 2) {
+        // thread item: column pair (c, c+1) x VEC tokens -> two 16-byte chunks
+        const int npair = (ncols + 1) / 2;
+        for (int it = threadIdx.x; it < npair * NCH; it += kThr) {
+            const int cp = it % npair, q = it / npair;
+            const int c = 2 * cp;
+            uint32_t v[VEC];
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) {
+                const int t = q * VEC + u;
+                // ncols is even (checked at launch), so the pair (c, c+1) is in range
+                v[u] = t < tn ? *reinterpret_cast<const uint32_t *>(src + (row0 + t) * ld + c0 + c) : 0u;
+            }
+            uint4 lo, hi;
+            uint32_t *pl = reinterpret_cast<uint32_t *>(&lo), *ph = reinterpret_cast<uint32_t *>(&hi);
+#pragma unroll
+            for (int u = 0; u < VEC / 2; ++u) {
+                pl[u] = __byte_perm(v[2 * u], v[2 * u + 1], 0x5410);
+                ph[u] = __byte_perm(v[2 * u], v[2 * u + 1], 0x7632);
+            }
+            const int sw0 = q ^ ((c >> 1) & (NCH - 1));
+            *reinterpret_cast<uint4 *>(dst + (size_t)c * kTC + sw0 * VEC) = lo;
+            if (c + 1 < ncols) {
+                const int sw1 = q ^ (((c + 1) >> 1) & (NCH - 1));
+                *reinterpret_cast<uint4 *>(dst + (size_t)(c + 1) * kTC + sw1 * VEC) = hi;
+            }
+        }
+    } else {
+        for (int it = threadIdx.x; it < ncols * NCH; it += kThr) {
+            const int c = it % ncols, q = it / ncols;
+            float4 v;
+            float *pv = reinterpret_cast<float *>(&v);
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) {
+                const int t = q * VEC + u;
+                pv[u] = t < tn ? to_f(src[(row0 + t) * ld + c0 + c]) : 0.0f;
+            }
+            const int sw = q ^ ((c >> 1) & (NCH - 1));
+            *reinterpret_cast<float4 *>(dst + (size_t)c * kTC + sw * VEC) = v;
+        }
+    }
+}
+
+template <typename Act>
+__device__ __forceinline__ void load_staged(const Act *row_base, int c, float (&out)[kTC]) {
+    constexpr int VEC = 16 / sizeof(Act);
+    constexpr int NCH = kTC / VEC;
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        const int sw = q ^ ((c >> 1) & (NCH - 1));
+        uint4 v = *reinterpret_cast<const uint4 *>(row_base + sw * VEC);
+        const uint32_t *pv = reinterpret_cast<const uint32_t *>(&v);
+        if (sizeof(Act) == 2) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                out[q * VEC + 2 * u] = __uint_as_float(pv[u] << 16);
+                out[q * VEC + 2 * u + 1] = __uint_as_float(pv[u] & 0xFFFF0000u);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) out[q * VEC + u] = __uint_as_float(pv[u]);
+        }
+    }
+}
+
+// Work item = (row block of 512 storage rows, expert).  Per 32-token chunk
+// the block stages gin (all C columns) and gout (its 512 columns) transposed
+// in shared memory; each thread owns 2 rows and walks their CSR entries,
+// dotting 32 staged tokens per entry; per-entry partial sums go to scratch
+// (one owner per entry, fixed chunk order -> deterministic).
+template <typename Act>
+__global__ void __launch_bounds__(kThr) sddmm_kernel(usaf_route_plan pl, usaf_qweight w,
+                                                     const Act *__restrict__ gout,
+                                                     const Act *__restrict__ gin,
+                                                     const int32_t *__restrict__ csr_to_compact,
+                                                     float scale, float *__restrict__ compact,
+                                                     float *__restrict__ scratch) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    Act *ginT = reinterpret_cast<Act *>(smem_raw);              // [C][TC]
-    Act *goutT = ginT + (size_t)w.C * TC;                       // [256][TC]
+    Act *ginT = reinterpret_cast<Act *>(smem_raw);               // [C][kTC]
+    Act *goutT = ginT + (size_t)w.C * kTC;                       // [kRowsPerBlock][kTC]
     const int e = blockIdx.y;
     const int R = w.R, C = w.C;
     const int cnt = pl.expert_cnt[e];
     if (cnt == 0) return;
-    const int seg0 = pl.expert_off[e];
-    const int r_local = threadIdx.x;
-    const int r = blockIdx.x * kRowsPerBlock + r_local;
-    const int rows_here = min(kRowsPerBlock, R - (int)blockIdx.x * kRowsPerBlock);
-    int jb = 0, je = 0;
-    if (r < R) {
-        jb = w.row_ptr[(int64_t)e * R + r];
-        je = w.row_ptr[(int64_t)e * R + r + 1];
-    }
-    for (int t0 = 0; t0 < cnt; t0 += TC) {
-        int tn = min(TC, cnt - t0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < TC * C; i += blockDim.x) {
-            int t = i / C, c = i - t * C;
-            ginT[(size_t)c * TC + t] =
-                t < tn ? gin[(int64_t)(seg0 + t0 + t) * C + c] : from_f<Act>(0.0f);
-        }
-        for (int i = threadIdx.x; i < TC * rows_here; i += blockDim.x) {
-            int t = i / rows_here, rr = i - t * rows_here;
-            goutT[(size_t)rr * TC + t] =
-                t < tn ? gout[(int64_t)(seg0 + t0 + t) * R + blockIdx.x * kRowsPerBlock + rr]
-                       : from_f<Act>(0.0f);
-        }
-        __syncthreads();
-        if (r < R && jb < je) {
-            float a[TC];
+    const int64_t seg0 = pl.expert_off[e];
+    const int rb0 = blockIdx.x * kRowsPerBlock;
+    const int rows_here = min(kRowsPerBlock, R - rb0);
+    int jb[2], je[2];
 #pragma unroll
-            for (int t = 0; t < TC; ++t) a[t] = to_f(goutT[(size_t)r_local * TC + t]);
-            for (int j = jb; j < je; ++j) {
-                const Act *col = ginT + (size_t)w.col[j] * TC;
+    for (int h = 0; h < 2; ++h) {
+        const int rr = threadIdx.x + h * kThr;
+        jb[h] = je[h] = 0;
+        if (rr < rows_here) {
+            jb[h] = w.row_ptr[(int64_t)e * R + rb0 + rr];
+            je[h] = w.row_ptr[(int64_t)e * R + rb0 + rr + 1];
+        }
+    }
+    for (int t0 = 0; t0 < cnt; t0 += kTC) {
+        const int tn = min(kTC, cnt - t0);
+        __syncthreads();
+        stage_transposed<Act>(gin, C, seg0 + t0, tn, 0, C, ginT);
+        stage_transposed<Act>(gout, R, seg0 + t0, tn, rb0, rows_here, goutT);
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (jb[h] >= je[h]) continue;
+            const int rr = threadIdx.x + h * kThr;
+            float a[kTC];
+            load_staged<Act>(goutT + (size_t)rr * kTC, rr, a);
+            for (int j = jb[h]; j < je[h]; ++j) {
+                const int c = w.col[j];
+                float b[kTC];
+                load_staged<Act>(ginT + (size_t)c * kTC, c, b);
                 float d = 0.0f;
 #pragma unroll
-                for (int t = 0; t < TC; ++t) d = fmaf(a[t], to_f(col[t]), d);
+                for (int t = 0; t < kTC; ++t) d = fmaf(a[t], b[t], d);
                 scratch[j] = t0 == 0 ? d : __fadd_rn(scratch[j], d);
             }
         }
     }
-    if (r < R) {
-        for (int j = jb; j < je; ++j) {
-            int pos = csr_to_compact[j];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        for (int j = jb[h]; j < je[h]; ++j) {
+            const int pos = csr_to_compact[j];
             compact[pos] = __fadd_rn(compact[pos], __fmul_rn(scale, round_to<Act>(scratch[j])));
         }
     }
@@ -125,23 +208,15 @@ template <typename Act>
 static int sddmm_launch(const usaf_route_plan *pl, const usaf_qweight *w, const Act *gout,
                         const Act *gin, const int32_t *c2c, float scale, float *compact,
                         float *scratch, cudaStream_t st) {
-    const size_t budget = 200 * 1024;
+    const size_t bytes = ((size_t)w->C + kRowsPerBlock) * kTC * sizeof(Act);
+    if (bytes > 220 * 1024 || (w->C & 1) || (w->R & 1)) return USAF_EUNSUPPORTED;
+    if (cudaFuncSetAttribute(sddmm_kernel<Act>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)bytes) != cudaSuccess)
+        return USAF_ECUDA;
     dim3 grid(cdiv(w->R, kRowsPerBlock), w->E);
-    auto bytes = [&](int tc) { return ((size_t)w->C + kRowsPerBlock) * tc * sizeof(Act); };
-#define SDDMM_TRY(TC)                                                                            \
-    if (bytes(TC) <= budget) {                                                                   \
-        cudaFuncSetAttribute(sddmm_kernel<Act, TC>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)bytes(TC));                                                    \
-        sddmm_kernel<Act, TC><<<grid, kRowsPerBlock, bytes(TC), st>>>(*pl, *w, gout, gin, c2c,   \
-                                                                      scale, compact, scratch);  \
-        USAF_CHECK_LAUNCH();                                                                     \
-        return USAF_OK;                                                                          \
-    }
-    SDDMM_TRY(32)
-    SDDMM_TRY(16)
-    SDDMM_TRY(8)
-#undef SDDMM_TRY
-    return USAF_EUNSUPPORTED;
+    sddmm_kernel<Act><<<grid, kThr, bytes, st>>>(*pl, *w, gout, gin, c2c, scale, compact, scratch);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
 }
 
 }  // namespace usaf
