@@ -181,6 +181,21 @@ int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w, const voi
                    const void *gin, int32_t dtype, const int32_t *csr_to_compact,
                    float scale, float *compact, float *scratch, void *stream);
 
+/* usaf_sparse_dw_noalloc: usaf_sparse_dw for callers that cannot allocate
+ * device memory at call time (a process working inside a pool it reserved at
+ * start-up, or a foreign-language host that can only pass buffers it already
+ * owns).  No counterpart in the reference.  The per-coordinate scratch is a
+ * fixed array inside this library (2,097,152 fp32 slots = 8 MiB, resident on
+ * every GPU that loads the library until exit); a projection with more
+ * overlay coordinates returns USAF_EUNSUPPORTED.  The first call on a device
+ * looks the array up (cudaGetSymbolAddress) with that device current, so make
+ * that first call before any stream capture.  All calls share the one array:
+ * calls that may overlap on the GPU (different streams, several threads)
+ * race and must be serialized by the caller.  Allocates nothing. */
+int usaf_sparse_dw_noalloc(const usaf_route_plan *plan, const usaf_qweight *w, const void *gout,
+                           const void *gin, int32_t dtype, const int32_t *csr_to_compact,
+                           float scale, float *compact, void *stream);
+
 /* ---- optimizer ------------------------------------------------------------
  * usaf_sparse_adam replaces SparseAdam.step (usaf/sparse_optim.py:86-134) in
  * compact mode: p = fp32 master [n]; m, v fp32 [n]; grad fp32 [n] (divided by

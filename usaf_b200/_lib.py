@@ -52,6 +52,7 @@ _SIGS = {
     "usaf_expert_down_bwd": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, P, I32, P, P]),
     "usaf_expert_gate_up_bwd": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, I32, P, P]),
     "usaf_sparse_dw": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, P, I32, P, F32T, P, P, P]),
+    "usaf_sparse_dw_noalloc": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, P, I32, P, F32T, P, P]),
     "usaf_expert_dense_dw": (I32, [C.POINTER(RoutePlan), I32, I32, P, P, I32, P, P]),
     "usaf_sparse_adam": (I32, [I64, P, P, P, P, F64, I32, F64, F64, F64, F64, F64, I32, P, P, P, P, P]),
     "usaf_sparse_adam_gather": (I32, [I64, P, P, P, I32, F64, P, P, I32, F64, F64, F64, F64, F64, P]),

@@ -251,3 +251,57 @@ extern "C" int usaf_expert_dense_dw(const usaf_route_plan *plan, int32_t R, int3
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
+
+// ---- allocation-free variant -------------------------------------------------
+// usaf_sparse_dw needs an fp32 scratch vector with one slot per selected
+// coordinate.  Some callers cannot allocate device memory when they call in:
+// code that runs inside a fixed, pre-reserved memory budget (a serving process
+// whose pool is carved up at start-up), or a foreign-language host that only
+// hands over buffers it registered earlier and has no binding for cudaMalloc.
+// usaf_sparse_dw_noalloc serves them with a scratch array that lives in this
+// library's own device memory: a file-scope __device__ array of
+// kNoAllocScratchFloats floats (8 MiB), resident on every GPU that loads the
+// library until the process exits.
+namespace usaf {
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 21;  // 2,097,152 coordinates
+}  // namespace usaf
+
+static __device__ __align__(256) float g_sddmm_noalloc_scratch[usaf::kNoAllocScratchFloats];
+
+// Device address of the scratch array on the current device.  The host-side
+// symbol is only a stand-in, so the address is looked up once per device
+// (with that device current) and cached.
+static float *noalloc_scratch_ptr(int *status) {
+    constexpr int kMaxDevices = 64;
+    static float *addr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        *status = USAF_ECUDA;
+        return nullptr;
+    }
+    if (!addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_sddmm_noalloc_scratch) != cudaSuccess || !p) {
+            (void)cudaGetLastError();
+            *status = USAF_ECUDA;
+            return nullptr;
+        }
+        addr[dev] = static_cast<float *>(p);
+    }
+    *status = USAF_OK;
+    return addr[dev];
+}
+
+extern "C" int usaf_sparse_dw_noalloc(const usaf_route_plan *plan, const usaf_qweight *w,
+                                      const void *gout, const void *gin, int32_t dtype,
+                                      const int32_t *csr_to_compact, float scale, float *compact,
+                                      void *stream) {
+    USAF_REQUIRE(plan && w);
+    if (w->n_ov > usaf::kNoAllocScratchFloats) return USAF_EUNSUPPORTED;  // beyond the built-in scratch
+    int rc = USAF_OK;
+    float *scratch = noalloc_scratch_ptr(&rc);
+    if (rc != USAF_OK) return rc;
+    // every slot the kernel reads is written first (first token chunk stores,
+    // later chunks add), so the previous call's contents need no clearing
+    return usaf_sparse_dw(plan, w, gout, gin, dtype, csr_to_compact, scale, compact, scratch, stream);
+}
