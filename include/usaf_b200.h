@@ -108,10 +108,12 @@ int usaf_int4_transpose(const void *q, const void *s, const void *z, int32_t E, 
  * than k), renormalisation, weights cast to the activation dtype.
  * logits/probs: fp32 [T,E]; wsum: fp32 [T] (the renormaliser); weights:
  * activation dtype [T,E].
- * usaf_router_select runs the same selection from given logits. */
+ * usaf_router_select runs the same selection from given logits.
+ * ws: usaf_router_workspace_bytes(T, H, E) bytes or NULL; err: device error word. */
 int usaf_router_fwd(const void *x, const void *w_r, int32_t dtype, int32_t T, int32_t H,
                     int32_t E, int32_t top_k, int32_t norm_topk_prob, float *logits,
-                    float *probs, float *wsum, void *weights, void *stream);
+                    float *probs, float *wsum, void *weights, void *ws, int32_t *err,
+                    void *stream);
 int usaf_router_select(const float *logits, int32_t dtype, int32_t T, int32_t E,
                        int32_t top_k, int32_t norm_topk_prob, float *probs, float *wsum,
                        void *weights, void *stream);
@@ -124,7 +126,11 @@ int usaf_router_select(const float *logits, int32_t dtype, int32_t T, int32_t E,
 int usaf_router_bwd(const usaf_route_plan *plan, const void *x, const void *w_r,
                     int32_t dtype, int32_t H, int32_t norm_topk_prob, const float *probs,
                     const float *wsum, const void *weights, const float *dw_pair,
-                    float *dlogits, void *dw_r, float *dx_acc, void *stream);
+                    float *dlogits, void *dw_r, float *dx_acc, void *ws, void *stream);
+/* Workspace of the router GEMMs (bf16 runs them on tensor cores: logits,
+ * dX_r and dW_r with split-K partials summed in a fixed order).  ws may be
+ * NULL (CUDA-core path); err receives device-side wait timeouts. */
+int64_t usaf_router_workspace_bytes(int32_t T, int32_t H, int32_t E);
 
 /* ---- dispatch / combine ---------------------------------------------------
  * usaf_dispatch replaces the nonzero / bincount / stable argsort / cumsum

@@ -82,7 +82,7 @@ def test_grouped_gemms_vs_torch(dev, case):
     st = _lib.stream()
     _lib.call("usaf_router_fwd", _lib.ptr(x), _lib.ptr(w_r), _lib.BF16, case["T"], case["H"],
               case["E"], case["k"], 1, _lib.ptr(blk.logits), _lib.ptr(blk.probs),
-              _lib.ptr(blk.wsum), _lib.ptr(blk.weights), st)
+              _lib.ptr(blk.wsum), _lib.ptr(blk.weights), _lib.ptr(blk.router_ws), _lib.ptr(blk.err), st)
     _lib.call("usaf_dispatch", blk.plan, _lib.ptr(blk.weights), _lib.ptr(x), _lib.BF16, case["H"],
               _lib.ptr(blk.x_perm), st)
     _lib.call("usaf_expert_gate_up_fwd", blk.plan, p["gate_up_proj"].struct(), _lib.ptr(blk.x_perm),

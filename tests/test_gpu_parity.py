@@ -119,7 +119,7 @@ def test_router_ties_fixture(dev, golden_dir):
     wt = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
     xd, wd = x.to(dev), w_r.to(dev)  # device copies must outlive the launch
     _lib.call("usaf_router_fwd", _lib.ptr(xd), _lib.ptr(wd), _lib.BF16, T, H, E,
-              t["k"], 1, _lib.ptr(lg), _lib.ptr(pr), _lib.ptr(ws), _lib.ptr(wt), _lib.stream())
+              t["k"], 1, _lib.ptr(lg), _lib.ptr(pr), _lib.ptr(ws), _lib.ptr(wt), None, None, _lib.stream())
     assert torch.equal(wt.cpu() != 0, t["weights"] != 0)
     assert int((wt.cpu() != 0).sum(1).max()) > t["k"]
 

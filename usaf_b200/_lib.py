@@ -40,9 +40,10 @@ _SIGS = {
     "usaf_dequant_int4": (I32, [P, P, P, I64, I32, I32, P, P]),
     "usaf_quant_int4": (I32, [P, I32, I64, I32, P, P, P, P]),
     "usaf_int4_transpose": (I32, [P, P, P, I32, I32, I32, I32, P, P, P]),
-    "usaf_router_fwd": (I32, [P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, P]),
+    "usaf_router_fwd": (I32, [P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, P, P, P]),
+    "usaf_router_workspace_bytes": (I64, [I32, I32, I32]),
     "usaf_router_select": (I32, [P, I32, I32, I32, I32, I32, P, P, P, P]),
-    "usaf_router_bwd": (I32, [C.POINTER(RoutePlan), P, P, I32, I32, I32, P, P, P, P, P, P, P, P]),
+    "usaf_router_bwd": (I32, [C.POINTER(RoutePlan), P, P, I32, I32, I32, P, P, P, P, P, P, P, P, P]),
     "usaf_dispatch": (I32, [C.POINTER(RoutePlan), P, P, I32, I32, P, P]),
     "usaf_combine": (I32, [C.POINTER(RoutePlan), P, I32, I32, P, P]),
     "usaf_combine_bwd": (I32, [C.POINTER(RoutePlan), P, P, I32, I32, P, P, P]),

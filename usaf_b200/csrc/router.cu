@@ -151,7 +151,8 @@ __global__ void __launch_bounds__(256) router_bwd_token(
     const int32_t *__restrict__ tok_off, const int32_t *__restrict__ pair_exp,
     const float *__restrict__ dw_pair, const float *__restrict__ probs,
     const float *__restrict__ wsum, const Act *__restrict__ weights, int T, int E, int norm,
-    float *__restrict__ dlogits) {
+    float *__restrict__ dlogits, __nv_bfloat16 *__restrict__ dl_bf, __nv_bfloat16 *__restrict__ dlT,
+    int ldT) {
     int lane = threadIdx.x & 31;
     int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (t >= T) return;
@@ -198,7 +199,12 @@ __global__ void __launch_bounds__(256) router_bwd_token(
 #pragma unroll
     for (int j = 0; j < EPL; ++j) {
         int e = lane + 32 * j;
-        if (e < E) dlogits[(int64_t)t * E + e] = round_to<Act>(__fmul_rn(__fsub_rn(dp[j], sdp), p[j]));
+        if (e < E) {
+            const float d = round_to<Act>(__fmul_rn(__fsub_rn(dp[j], sdp), p[j]));
+            dlogits[(int64_t)t * E + e] = d;
+            if (dl_bf) dl_bf[(int64_t)t * E + e] = __float2bfloat16_rn(d);
+            if (dlT) dlT[(int64_t)e * ldT + t] = __float2bfloat16_rn(d);
+        }
     }
     (void)weights;
 }
@@ -244,10 +250,11 @@ static int launch_select(const float *logits, int T, int E, int k, int norm, flo
 template <typename Act>
 static int launch_router_bwd_token(const usaf_route_plan *pl, const float *dw_pair,
                                    const float *probs, const float *wsum, const Act *w, int norm,
-                                   float *dl, cudaStream_t st) {
+                                   float *dl, __nv_bfloat16 *dl_bf, __nv_bfloat16 *dlT, int ldT,
+                                   cudaStream_t st) {
     int T = pl->T, E = pl->E;
     unsigned grid = cdiv((int64_t)T * 32, 256);
-#define RB_LAUNCH(EPL) router_bwd_token<Act, EPL><<<grid, 256, 0, st>>>(pl->tok_off, pl->pair_exp, dw_pair, probs, wsum, w, T, E, norm, dl)
+#define RB_LAUNCH(EPL) router_bwd_token<Act, EPL><<<grid, 256, 0, st>>>(pl->tok_off, pl->pair_exp, dw_pair, probs, wsum, w, T, E, norm, dl, dl_bf, dlT, ldT)
     if (E <= 32) RB_LAUNCH(1);
     else if (E <= 64) RB_LAUNCH(2);
     else if (E <= 128) RB_LAUNCH(4);
@@ -257,6 +264,82 @@ static int launch_router_bwd_token(const usaf_route_plan *pl, const float *dw_pa
 #undef RB_LAUNCH
     USAF_CHECK_LAUNCH();
     return USAF_OK;
+}
+
+
+// ---- tensor-core path (bf16): transposes and split-K finalize -------------
+int dense_tc_partials(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda,
+                      const __nv_bfloat16 *B, int b_rows, int b_cols, int ldb, int Mp, int Np,
+                      int Kp, int splits, float *part, int *err, cudaStream_t st);
+bool dense_tc_available();
+
+static inline int64_t rup(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// dst[c][r] = src[r][c] for a [rows, cols] bf16 matrix (dst row stride ldd)
+__global__ void transpose_bf16(const __nv_bfloat16 *__restrict__ src, int rows, int cols,
+                               __nv_bfloat16 *__restrict__ dst, int ldd) {
+    __shared__ __nv_bfloat16 tile[32][33];
+    int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        int r = r0 + i, c = c0 + threadIdx.x;
+        tile[i][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * cols + c] : __float2bfloat16_rn(0.f);
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+        int c = c0 + i, r = r0 + threadIdx.x;
+        if (c < cols && r < rows) dst[(int64_t)c * ldd + r] = tile[threadIdx.x][i];
+    }
+}
+
+// out[m][n] = round(sum_s part[s][m][n]) in split order; optional transpose
+// (out[n][m]); rounding to bf16 kept as fp32 (logits), bf16 storage (dW_r)
+// or none (dX_r accumulator).
+enum { FIN_F32_ROUND_BF16 = 0, FIN_BF16 = 1, FIN_F32 = 2 };
+__global__ void finalize_partials(const float *__restrict__ part, int splits, int Mp, int Np, int M,
+                                  int N, int transpose, int mode, void *out, int ldo) {
+    int64_t total = (int64_t)M * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t m, n, o;
+        if (transpose) { n = i / M; m = i % M; o = n * ldo + m; }   // coalesced output writes
+        else { m = i / N; n = i % N; o = m * ldo + n; }
+        float acc = 0.0f;
+        for (int s_ = 0; s_ < splits; ++s_) acc = __fadd_rn(acc, part[((int64_t)s_ * Mp + m) * Np + n]);
+        if (mode == FIN_F32_ROUND_BF16) reinterpret_cast<float *>(out)[o] = __bfloat162float(__float2bfloat16_rn(acc));
+        else if (mode == FIN_BF16) reinterpret_cast<__nv_bfloat16 *>(out)[o] = __float2bfloat16_rn(acc);
+        else reinterpret_cast<float *>(out)[o] = acc;
+    }
+}
+
+struct RouterWs {
+    float *part;
+    __nv_bfloat16 *xT, *wT, *dl_bf, *dlT;
+    int64_t Tp;
+};
+
+static int64_t router_ws_bytes(int T, int H, int E) {
+    int64_t Tp = rup(T, 128), Hp = rup(H, 128), Ep = rup(E, 128);
+    int64_t part = std::max({(int64_t)4 * Tp * Ep, Hp * Tp, (int64_t)8 * Ep * Hp});
+    return part * 4 + (Hp * Tp + Hp * Ep + Tp * Ep + Ep * Tp) * 2 + 5 * 256;
+}
+
+static RouterWs carve(void *ws, int T, int H, int E) {
+    int64_t Tp = rup(T, 128), Hp = rup(H, 128), Ep = rup(E, 128);
+    int64_t part = std::max({(int64_t)4 * Tp * Ep, Hp * Tp, (int64_t)8 * Ep * Hp});
+    char *p = static_cast<char *>(ws);
+    auto take = [&](int64_t bytes) { char *r = p; p += (bytes + 255) / 256 * 256; return r; };
+    RouterWs w;
+    w.part = reinterpret_cast<float *>(take(part * 4));
+    w.xT = reinterpret_cast<__nv_bfloat16 *>(take(Hp * Tp * 2));
+    w.wT = reinterpret_cast<__nv_bfloat16 *>(take(Hp * Ep * 2));
+    w.dl_bf = reinterpret_cast<__nv_bfloat16 *>(take(Tp * Ep * 2));
+    w.dlT = reinterpret_cast<__nv_bfloat16 *>(take(Ep * Tp * 2));
+    w.Tp = Tp;
+    return w;
+}
+
+static bool router_tc_ok(int T, int H, int E, const void *ws) {
+    return ws && dense_tc_available() && H % 64 == 0 && E % 64 == 0 && T >= 1;
 }
 
 }  // namespace usaf
@@ -277,12 +360,30 @@ extern "C" int usaf_router_select(const float *logits, int32_t dtype, int32_t T,
     }
 }
 
+extern "C" int64_t usaf_router_workspace_bytes(int32_t T, int32_t H, int32_t E) {
+    if (T < 0 || H < 1 || E < 1) return -1;
+    return router_ws_bytes(T, H, E);
+}
+
 extern "C" int usaf_router_fwd(const void *x, const void *w_r, int32_t dtype, int32_t T, int32_t H,
                                int32_t E, int32_t top_k, int32_t norm, float *logits,
-                               float *probs, float *wsum, void *weights, void *stream) {
+                               float *probs, float *wsum, void *weights, void *ws, int32_t *err,
+                               void *stream) {
     USAF_REQUIRE(x && w_r && logits && T >= 0 && H >= 1 && E >= 1);
     if (T == 0) return USAF_OK;
     cudaStream_t st = as_stream(stream);
+    if (dtype == USAF_BF16 && err && router_tc_ok(T, H, E, ws)) {
+        // logits = X W_r^T on tensor cores (split-K 4, fixed-order finalize)
+        RouterWs w = carve(ws, T, H, E);
+        int64_t Tp = rup(T, 128), Ep = rup(E, 128);
+        int rc = dense_tc_partials((const __nv_bfloat16 *)x, T, H, H, (const __nv_bfloat16 *)w_r, E, H, H,
+                                   (int)Tp, (int)Ep, H, 4, w.part, err, st);
+        if (rc) return rc;
+        finalize_partials<<<cdiv((int64_t)T * E, 256), 256, 0, st>>>(w.part, 4, (int)Tp, (int)Ep, T, E, 0,
+                                                                     FIN_F32_ROUND_BF16, logits, E);
+        USAF_CHECK_LAUNCH();
+        return usaf_router_select(logits, dtype, T, E, top_k, norm, probs, wsum, weights, stream);
+    }
     dim3 grid(cdiv(E, 64), cdiv(T, 64));
     switch (dtype) {
         case USAF_F32: logits_kernel<float><<<grid, 256, 0, st>>>((const float *)x, (const float *)w_r, T, H, E, logits); break;
@@ -296,22 +397,48 @@ extern "C" int usaf_router_fwd(const void *x, const void *w_r, int32_t dtype, in
 extern "C" int usaf_router_bwd(const usaf_route_plan *plan, const void *x, const void *w_r,
                                int32_t dtype, int32_t H, int32_t norm, const float *probs,
                                const float *wsum, const void *weights, const float *dw_pair,
-                               float *dlogits, void *dw_r, float *dx_acc, void *stream) {
+                               float *dlogits, void *dw_r, float *dx_acc, void *ws, void *stream) {
     USAF_REQUIRE(plan && x && w_r && probs && wsum && dw_pair && dlogits && dw_r && dx_acc);
     int T = plan->T, E = plan->E;
     if (T == 0) return USAF_OK;
     cudaStream_t st = as_stream(stream);
     int rc;
+    if (dtype == USAF_BF16 && router_tc_ok(T, H, E, ws)) {
+        RouterWs w = carve(ws, T, H, E);
+        const int64_t Tp = w.Tp, Hp = rup(H, 128), Ep = rup(E, 128);
+        const auto *xb = (const __nv_bfloat16 *)x;
+        const auto *wb = (const __nv_bfloat16 *)w_r;
+        rc = launch_router_bwd_token<__nv_bfloat16>(plan, dw_pair, probs, wsum, (const __nv_bfloat16 *)weights,
+                                                    norm, dlogits, w.dl_bf, w.dlT, (int)Tp, st);
+        if (rc) return rc;
+        // X^T [H][Tp] and W_r^T [H][E]
+        transpose_bf16<<<dim3(cdiv(H, 32), cdiv(T, 32)), dim3(32, 8), 0, st>>>(xb, T, H, w.xT, (int)Tp);
+        transpose_bf16<<<dim3(cdiv(H, 32), cdiv(E, 32)), dim3(32, 8), 0, st>>>(wb, E, H, w.wT, E);
+        USAF_CHECK_LAUNCH();
+        // dX_r^T [H][T] = W_r^T [H][E] * dl[T][E]^T   (K = E)
+        rc = dense_tc_partials(w.wT, H, E, E, w.dl_bf, T, E, E, (int)Hp, (int)Tp, E, 1, w.part, plan->err, st);
+        if (rc) return rc;
+        finalize_partials<<<cdiv((int64_t)T * H, 256), 256, 0, st>>>(w.part, 1, (int)Hp, (int)Tp, H, T, 1,
+                                                                     FIN_F32, dx_acc, H);
+        // dW_r [E][H] = dl^T [E][T] * X^T [H][T]^T   (K = T, split-K 8)
+        rc = dense_tc_partials(w.dlT, E, T, (int)Tp, w.xT, H, T, (int)Tp, (int)Ep, (int)Hp, (int)rup(T, 64), 8,
+                               w.part, plan->err, st);
+        if (rc) return rc;
+        finalize_partials<<<cdiv((int64_t)E * H, 256), 256, 0, st>>>(w.part, 8, (int)Ep, (int)Hp, E, H, 0,
+                                                                     FIN_BF16, dw_r, H);
+        USAF_CHECK_LAUNCH();
+        return USAF_OK;
+    }
     dim3 gw(cdiv(H, 64), cdiv(E, 64)), gx(cdiv(H, 64), cdiv(T, 64));
     switch (dtype) {
         case USAF_F32:
-            rc = launch_router_bwd_token<float>(plan, dw_pair, probs, wsum, (const float *)weights, norm, dlogits, st);
+            rc = launch_router_bwd_token<float>(plan, dw_pair, probs, wsum, (const float *)weights, norm, dlogits, nullptr, nullptr, 0, st);
             if (rc) return rc;
             dwr_kernel<float><<<gw, 256, 0, st>>>(dlogits, (const float *)x, T, H, E, (float *)dw_r);
             dxr_kernel<float><<<gx, 256, 0, st>>>(dlogits, (const float *)w_r, T, H, E, dx_acc);
             break;
         case USAF_BF16:
-            rc = launch_router_bwd_token<__nv_bfloat16>(plan, dw_pair, probs, wsum, (const __nv_bfloat16 *)weights, norm, dlogits, st);
+            rc = launch_router_bwd_token<__nv_bfloat16>(plan, dw_pair, probs, wsum, (const __nv_bfloat16 *)weights, norm, dlogits, nullptr, nullptr, 0, st);
             if (rc) return rc;
             dwr_kernel<__nv_bfloat16><<<gw, 256, 0, st>>>(dlogits, (const __nv_bfloat16 *)x, T, H, E, (__nv_bfloat16 *)dw_r);
             dxr_kernel<__nv_bfloat16><<<gx, 256, 0, st>>>(dlogits, (const __nv_bfloat16 *)w_r, T, H, E, dx_acc);

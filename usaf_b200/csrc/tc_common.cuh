@@ -63,7 +63,7 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
 // abort word so every role stops issuing new work.
 constexpr uint64_t kWaitBudgetNs = 2000000000ull;
 
-__device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity,
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity,
                                             volatile int *abort_flag, int *err) {
     uint64_t t0 = globaltimer();
     while (true) {

@@ -237,6 +237,8 @@ class MoEBlock:
         self.dx_acc = torch.empty(T, H, **f32)
         self.dx = torch.empty(T, H, **act)
         self.dw_r = torch.empty(E, H, **act)
+        self.router_ws = torch.empty(max(int(_lib.LIB.usaf_router_workspace_bytes(T, H, E)), 256),
+                                     dtype=torch.uint8, device=dev)
         self.plan = _lib.RoutePlan()
         p = self.plan
         p.T, p.E, p.P_cap = T, E, Pc
@@ -251,7 +253,7 @@ class MoEBlock:
         st = stream()
         call("usaf_router_fwd", ptr(x), ptr(w_r), self.dtc, d.T, d.H, d.E, d.top_k,
              int(d.norm_topk_prob), ptr(self.logits), ptr(self.probs), ptr(self.wsum),
-             ptr(self.weights), st)
+             ptr(self.weights), ptr(self.router_ws), ptr(self.err), st)
         call("usaf_dispatch", self.plan, ptr(self.weights), ptr(x), self.dtc, d.H,
              ptr(self.x_perm), st)
         call("usaf_expert_gate_up_fwd", self.plan, gu.struct(), ptr(self.x_perm), self.dtc,
@@ -271,7 +273,8 @@ class MoEBlock:
              ptr(self.dcur), ptr(self.dw_pair), st)
         call("usaf_router_bwd", self.plan, ptr(x), ptr(w_r), self.dtc, d.H,
              int(d.norm_topk_prob), ptr(self.probs), ptr(self.wsum), ptr(self.weights),
-             ptr(self.dw_pair), ptr(self.dlogits), ptr(self.dw_r), ptr(self.dx_acc), st)
+             ptr(self.dw_pair), ptr(self.dlogits), ptr(self.dw_r), ptr(self.dx_acc),
+             ptr(self.router_ws), st)
         call("usaf_expert_down_bwd", self.plan, dn.struct(), ptr(self.dcur), ptr(self.gu),
              self.dtc, ptr(self.dgu), st)
         call("usaf_expert_gate_up_bwd", self.plan, gu.struct(), ptr(self.dgu), self.dtc,
