@@ -62,26 +62,30 @@ typedef struct {
  * (usaf/quantization.py:21-85) with its sparse overlay of trained values
  * (usaf/moe_loader.py:241-247).  Storage shape [E, R, C], groups of
  * `group_size` consecutive elements along C (C % group_size == 0).
- * The overlay is held twice: CSR by storage row (row-major flat order) and
- * CSC by storage column, with values already rounded the way the reference
- * rounds them (fp16 of the master, then the compute dtype). */
+ * The overlay is held twice: CSR by storage row and CSC by storage column,
+ * each split into two sorted segments per row (column): entries whose
+ * column (row) index has bit 5 clear, then those with bit 5 set -- the two
+ * 32-wide halves of every 64-wide k-block.  Values are already rounded the
+ * way the reference rounds them (fp16 of the master, then the compute dtype). */
 typedef struct {
     int32_t E, R, C, group_size;
     const int8_t   *q;        /* [E*R*C/2] packed codes, low nibble = even element */
     const uint16_t *s;        /* [E*R*C/group_size] fp16 scales                   */
     const uint16_t *z;        /* [E*R*C/group_size] fp16 zeros                    */
     int32_t n_ov;
-    const int32_t *row_ptr;   /* [E*R+1]  CSR offsets                              */
+    const int32_t *row_ptr;   /* [E*R*2+1] CSR offsets, segment (row, half)         */
     const int32_t *col;       /* [n_ov]   column of each CSR entry                 */
     const float   *val;       /* [n_ov]   effective value of each CSR entry        */
-    const int32_t *colT_ptr;  /* [E*C+1]  CSC offsets                              */
+    const int32_t *colT_ptr;  /* [E*C*2+1] CSC offsets, segment (column, half)      */
     const int32_t *rowT;      /* [n_ov]   row of each CSC entry                    */
     const float   *valT;      /* [n_ov]   effective value of each CSC entry        */
-    /* optional column-major copy for the backward GEMMs (usaf_int4_transpose):
-     * qT [E*C*R/2] codes of storage column c packed along rows, and
-     * szT [E*(C/group_size)*R] uint32 (scale | zero << 16) per (column group, row) */
+    /* copies for the tensor-core GEMMs, codes in the usaf_int4_repack order:
+     * qP [E*R*C/2] row-major (forward), qT [E*C*R/2] column-major (backward,
+     * usaf_int4_transpose), szT [E*(C/group_size)*R] uint32 (scale | zero << 16)
+     * per (column group, row) */
     const int8_t   *qT;
     const uint32_t *szT;
+    const int8_t   *qP;
 } usaf_qweight;
 
 /* ---- int4 format ---------------------------------------------------------
@@ -100,6 +104,12 @@ int usaf_quant_int4(const void *x, int32_t x_dtype, int64_t numel, int32_t group
  * zeros, re-laid so a storage column's codes are contiguous. */
 int usaf_int4_transpose(const void *q, const void *s, const void *z, int32_t E, int32_t R,
                         int32_t C, int32_t group_size, void *qT, void *szT, void *stream);
+
+/* usaf_int4_repack: copy of the packed codes with the nibbles of every 32-bit
+ * word (8 elements) reordered to e0 e2 e4 e6 e1 e3 e5 e7, the order the
+ * tensor-core producers dequantize from (numel % 8 == 0).  The backward copy
+ * of usaf_int4_transpose is written in the same order. */
+int usaf_int4_repack(const void *q, int64_t numel, void *qp, void *stream);
 
 /* ---- router ----------------------------------------------------------------
  * usaf_router_fwd replaces the router of dml_qwen3_moe_block_forward

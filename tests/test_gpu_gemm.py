@@ -50,7 +50,7 @@ def eff_weight(p):
     w = p.dequant(torch.float16).reshape(-1).clone()
     idx = torch.empty(p.n_ov, dtype=torch.long, device=w.device)
     # reconstruct the overlay flat indices from the CSR
-    rows = torch.repeat_interleave(torch.arange(p.E * p.R, device=w.device),
+    rows = torch.repeat_interleave(torch.arange(p.E * p.R * 2, device=w.device) // 2,
                                    (p.row_ptr[1:] - p.row_ptr[:-1]).long())
     idx = rows * p.C + p.col.long()
     w[idx] = p.val.to(torch.float16)

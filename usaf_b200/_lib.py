@@ -32,7 +32,7 @@ class QWeight(C.Structure):
     _fields_ = [("E", I32), ("R", I32), ("C", I32), ("group_size", I32),
                 ("q", P), ("s", P), ("z", P), ("n_ov", I32),
                 ("row_ptr", P), ("col", P), ("val", P),
-                ("colT_ptr", P), ("rowT", P), ("valT", P), ("qT", P), ("szT", P)]
+                ("colT_ptr", P), ("rowT", P), ("valT", P), ("qT", P), ("szT", P), ("qP", P)]
 
 
 # name -> (restype, argtypes)
@@ -40,6 +40,7 @@ _SIGS = {
     "usaf_dequant_int4": (I32, [P, P, P, I64, I32, I32, P, P]),
     "usaf_quant_int4": (I32, [P, I32, I64, I32, P, P, P, P]),
     "usaf_int4_transpose": (I32, [P, P, P, I32, I32, I32, I32, P, P, P]),
+    "usaf_int4_repack": (I32, [P, I64, P, P]),
     "usaf_router_fwd": (I32, [P, P, I32, I32, I32, I32, I32, I32, P, P, P, P, P, P, P]),
     "usaf_router_workspace_bytes": (I64, [I32, I32, I32]),
     "usaf_router_select": (I32, [P, I32, I32, I32, I32, I32, P, P, P, P]),

@@ -81,13 +81,14 @@ __global__ void __launch_bounds__(256) grouped_gemm_simt(usaf_route_plan pl, usa
         if (w.n_ov > 0 && threadIdx.x < BN) {
             int n = n0 + threadIdx.x;
             if (n < N) {
+                const int half = (k0 >> 5) & 1;   // the 16-wide k tile lies in one 32-wide half
                 if (!TRANS) {
-                    int r = e * R + n;
+                    int r = (e * R + n) * 2 + half;
                     int b = w.row_ptr[r], en = w.row_ptr[r + 1];
                     for (int j = lower_bound_i32(w.col, b, en, k0); j < en && w.col[j] < k0 + BK; ++j)
                         Ws[w.col[j] - k0][threadIdx.x] = w.val[j];
                 } else {
-                    int c = e * C + n;
+                    int c = (e * C + n) * 2 + half;
                     int b = w.colT_ptr[c], en = w.colT_ptr[c + 1];
                     for (int j = lower_bound_i32(w.rowT, b, en, k0); j < en && w.rowT[j] < k0 + BK; ++j)
                         Ws[w.rowT[j] - k0][threadIdx.x] = w.valT[j];

@@ -37,7 +37,7 @@ constexpr int kMaxTok = kSub * kMaxSub;          // 384 tokens per CTA
 constexpr int kSubBytes = kSub * kBK * 2;        // 16 KB per TMA box
 constexpr int kStageBytes = kMaxSub * kSubBytes; // 48 KB per stage
 constexpr int kAcol = kMaxTok;                   // first TMEM column of the A stages
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;                   // 0 TMA, 1 MMA, 4-11 dequant + epilogue
 constexpr int kStageLd = 136;                    // epilogue staging row stride (elements)
 
 enum : int { MODE_GATE_UP = 0, MODE_DOWN = 1, MODE_DOWN_BWD = 2, MODE_GU_BWD = 3 };
@@ -54,7 +54,7 @@ struct alignas(8) TcShared {
     int abort_flag;
 };
 
-constexpr size_t kStgBytes = (size_t)32 * kStageLd * 2;  // epilogue staging tile
+constexpr size_t kStgBytes = (size_t)2 * 32 * kStageLd * 2;  // epilogue staging, one per warp group
 constexpr size_t kSzBytes = (size_t)4 * kBK * 4;          // transposed-mode scale ring
 // stages + epilogue staging + scale ring + shared block + tile prefix / counts (E <= 1024)
 constexpr size_t kSmemBytes =
@@ -71,32 +71,45 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, int *
     }
 }
 
-__device__ __forceinline__ void dequant_block(uint4 a, uint4 b, uint16_t s_bits, uint16_t z_bits,
-                                              uint32_t (&r)[32]) {
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const __half2 s2 = __half2half2(__ushort_as_half(s_bits));
-    const __half2 z2 = __half2half2(__ushort_as_half(z_bits));
-    const __half2 magic = __half2half2(__ushort_as_half((unsigned short)0x6400));  // 1024
+// Dequantize 32 elements (16 pairs) from 4 code words in the repacked
+// order: pair i = nibbles (i%4, i%4+4) of word i/4.  fp16(fp16(q*s)+z) per
+// element (separately rounded multiply and add, the reference's rounding),
+// then bf16.  SCALE_PER_ROW: pair i has its own (scale, zero) per element
+// (transposed weights); otherwise one (scale, zero) for the whole block.
+// A pending trained coordinate at pair pj is blended in after the bf16
+// conversion (sel picks the half).
+template <bool SCALE_PER_ROW>
+__device__ __forceinline__ void dequant16(uint4 codes, uint32_t szw, const uint32_t *szr, int pj,
+                                          uint32_t m2, uint32_t sel, uint32_t (&r)[16]) {
+    const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
+    const __half2 magic = __half2half2(__ushort_as_half((unsigned short)0x6400));
+    __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFF)));
+    __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(szw >> 16)));
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        uint32_t byte = (w[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
-        uint32_t u = (byte & 0xFu) | ((byte & 0xF0u) << 12) | 0x64006400u;
-        __half2 c = __hsub2(*reinterpret_cast<__half2 *>(&u), magic);  // exact codes (lo, hi)
-        __half2 v = __hadd2_rn(__hmul2_rn(c, s2), z2);                  // fp16(fp16(q*s)+z)
+    for (int i = 0; i < 16; ++i) {
+        uint32_t u = ((w[i >> 2] >> (4 * (i & 3))) & 0x000F000Fu) | 0x64006400u;
+        __half2 c = __hsub2(*reinterpret_cast<__half2 *>(&u), magic);
+        if (SCALE_PER_ROW) {
+            uint32_t wa = szr[2 * i], wb = szr[2 * i + 1];
+            uint32_t su = __byte_perm(wa, wb, 0x5410), zu = __byte_perm(wa, wb, 0x7632);
+            s2 = *reinterpret_cast<__half2 *>(&su);
+            z2 = *reinterpret_cast<__half2 *>(&zu);
+        }
+        __half2 v = __hadd2_rn(__hmul2_rn(c, s2), z2);
         float2 f = __half22float2(v);
         __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
-        r[j] = *reinterpret_cast<uint32_t *>(&bb);
+        uint32_t rv = *reinterpret_cast<uint32_t *>(&bb);
+        r[i] = (i == pj) ? __byte_perm(rv, m2, sel) : rv;
     }
 }
 
-// Replace element c (0..63) of a packed bf16x2 block with the bf16 bits vb.
-// A predicated select per register keeps r[] in registers (an indexed write
-// would move the whole block to local memory).
-__device__ __forceinline__ void patch_elem(uint32_t (&r)[32], int c, uint32_t vb) {
+// slow path for a second trained coordinate in the same 32-wide block:
+// predicated select per register keeps r[] in registers
+__device__ __forceinline__ void patch_elem16(uint32_t (&r)[16], int c, uint32_t vb) {
     const uint32_t pi = (uint32_t)c >> 1;
     const bool hi = c & 1;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < 16; ++i) {
         const uint32_t cand = hi ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
         asm volatile("{\n .reg .pred p;\n setp.eq.u32 p, %1, %2;\n selp.b32 %0, %3, %0, p;\n}\n"
                      : "+r"(r[i])
@@ -104,30 +117,15 @@ __device__ __forceinline__ void patch_elem(uint32_t (&r)[32], int c, uint32_t vb
     }
 }
 
-// transposed-mode dequant: element pair j covers storage rows 2j, 2j+1 of one
-// column, each row with its own (scale, zero) from the staged scale block
-__device__ __forceinline__ void dequant_block_rows(uint4 a, uint4 b, const uint32_t *sz,
-                                                   uint32_t (&r)[32]) {
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const __half2 magic = __half2half2(__ushort_as_half((unsigned short)0x6400));
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        uint32_t byte = (w[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
-        uint32_t u = (byte & 0xFu) | ((byte & 0xF0u) << 12) | 0x64006400u;
-        __half2 c = __hsub2(*reinterpret_cast<__half2 *>(&u), magic);
-        uint32_t wa = sz[2 * j], wb = sz[2 * j + 1];
-        uint32_t s2u = __byte_perm(wa, wb, 0x5410), z2u = __byte_perm(wa, wb, 0x7632);
-        __half2 v = __hadd2_rn(__hmul2_rn(c, *reinterpret_cast<__half2 *>(&s2u)),
-                               *reinterpret_cast<__half2 *>(&z2u));
-        float2 f = __half22float2(v);
-        __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
-        r[j] = *reinterpret_cast<uint32_t *>(&bb);
-    }
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
 }
 
-// Work item = (token tile, row block); tile t of expert e covers tokens
-// [t0, t0+ntok) of e's segment.  Consecutive work items share a token tile
-// so its rows are reused from L2 across row blocks.
 __device__ __forceinline__ void decode_tile(const int *tile_off, const int *cnts, int E, int tile,
                                             int &e, int &t0, int &ntok) {
     int lo = 0, hi = E;  // first expert with tile_off[e+1] > tile
@@ -178,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int c4[4], n4[4], mine = 0;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            int e_ = tid * 4 + q;
+            int e_ = tid * 4 + q;   // 384 threads x 4 >= 1024 experts
             c4[q] = e_ < E ? pl.expert_cnt[e_] : 0;
             n4[q] = (c4[q] + kMaxTok - 1) / kMaxTok;
             mine += n4[q];
@@ -205,11 +203,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             S.abort_flag = 0;
             for (int st = 0; st < kStages; ++st) {
                 mbar_init(&S.full_b[st], 1);
-                mbar_init(&S.full_a[st], 128);
+                mbar_init(&S.full_a[st], 256);
                 mbar_init(&S.empty[st], 1);
             }
             mbar_init(&S.acc, 1);
-            mbar_init(&S.acc_empty, 128);
+            mbar_init(&S.acc_empty, 256);
             fence_barrier_init();
         }
     }
@@ -292,11 +290,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4) {
         // ---------------- dequant producers + epilogue ----------------
-        const int t = tid - 128;  // TMEM lane
+        // 8 warps: warp w owns TMEM lane quarter w%4 and K half hf of every
+        // 64-wide k-block (columns [hf*32, hf*32+32))
+        const int t = tid - 128;                // 0..255
+        const int row = t & 127;                // TMEM lane = weight row of the tile
+        const int hf = t >> 7;
         const uint32_t lane_off = ((uint32_t)(warp & 3) * 32) << 16;
         const int gs = w.group_size;
         const unsigned short *s_ptr = reinterpret_cast<const unsigned short *>(w.s);
         const unsigned short *z_ptr = reinterpret_cast<const unsigned short *>(w.z);
+        __nv_bfloat16 *stg_g = stg + hf * 32 * kStageLd;   // this group's staging tile
         int g = 0, it = 0;
         bool ok = true;
         for (int work = blockIdx.x; work < n_work && ok; work += gridDim.x, ++it) {
@@ -304,118 +307,127 @@ __global__ void __launch_bounds__(kThreads, 1)
             decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
             const int rb = work % nrb;
             const int row0 = pl.expert_off[e] + t0;
-            // code row of this lane, and where its output lives
-            int64_t crow;        // row index into q (fwd) or qT (bwd)
+            int64_t crow;        // row of q (fwd) or qT (bwd) this lane dequantizes
             int j0 = 0, h0 = 0;  // output column base
             if (MODE == MODE_GATE_UP) {
                 const int I = R / 2;
                 j0 = rb * 64;
-                crow = (int64_t)e * R + (t < 64 ? j0 + t : I + j0 + (t - 64));
+                crow = (int64_t)e * R + (row < 64 ? j0 + row : I + j0 + (row - 64));
             } else if (MODE == MODE_DOWN) {
                 h0 = rb * 128;
-                crow = (int64_t)e * R + h0 + t;
+                crow = (int64_t)e * R + h0 + row;
             } else {
                 h0 = rb * 128;   // storage column block
-                crow = (int64_t)e * C + h0 + t;
+                crow = (int64_t)e * C + h0 + row;
             }
-            const uint4 *qrow = reinterpret_cast<const uint4 *>((TRANS ? w.qT : w.q) + crow * (K / 2));
+            const uint4 *qrow = reinterpret_cast<const uint4 *>((TRANS ? w.qT : w.qP) + crow * (K / 2)) + hf;
             const int64_t gbase = crow * (int64_t)K;
-            int cur = 0, cend = 0, ncol = 0x7fffffff;
-            float nval = 0.0f;
+            // overlay queue of this lane: next two trained coordinates (K index, bf16 bits)
             const int32_t *ov_ptr = TRANS ? w.colT_ptr : w.row_ptr;
             const int32_t *ov_idx = TRANS ? w.rowT : w.col;
             const float *ov_val = TRANS ? w.valT : w.val;
+            int cur = 0, cend = 0, qc0 = 0x7fffffff, qc1 = 0x7fffffff;
+            uint32_t qv0 = 0, qv1 = 0;
             if (w.n_ov > 0) {
-                cur = ov_ptr[crow];
-                cend = ov_ptr[crow + 1];
-                if (cur < cend) { ncol = ov_idx[cur]; nval = ov_val[cur]; }
+                cur = ov_ptr[crow * 2 + hf];      // this lane's (row, half) segment
+                cend = ov_ptr[crow * 2 + hf + 1];
+                if (cur < cend) { qc0 = ov_idx[cur]; qv0 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur])); }
+                if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
             }
             // rolling 3-deep prefetch ring of (codes, scale|zero)
-            uint4 a0 = make_uint4(0, 0, 0, 0), b0 = a0, a1 = a0, b1 = a0, a2 = a0, b2 = a0;
+            uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, a2 = a0;
             uint32_t z0 = 0, z1 = 0, z2 = 0;
-#define USAF_LOAD(kb_, A_, B_, Z_)                                                               \
+#define USAF_LOAD(kb_, A_, Z_)                                                                   \
     do {                                                                                         \
         A_ = __ldg(qrow + (kb_) * 2);                                                            \
-        B_ = __ldg(qrow + (kb_) * 2 + 1);                                                        \
         if (!TRANS) {                                                                            \
             int64_t gg = (gbase + (int64_t)(kb_) * kBK) / gs;                                    \
             Z_ = (uint32_t)__ldg(s_ptr + gg) | ((uint32_t)__ldg(z_ptr + gg) << 16);              \
         }                                                                                        \
     } while (0)
-            USAF_LOAD(0, a0, b0, z0);
-            if (1 < nk) USAF_LOAD(1, a1, b1, z1);
-            if (2 < nk) USAF_LOAD(2, a2, b2, z2);
+            USAF_LOAD(0, a0, z0);
+            if (1 < nk) USAF_LOAD(1, a1, z1);
+            if (2 < nk) USAF_LOAD(2, a2, z2);
             for (int kb = 0; kb < nk; ++kb, ++g) {
-                uint4 na = a2, nb = b2;
+                uint4 na = a2;
                 uint32_t nz = z2;
-                if (kb + 3 < nk) USAF_LOAD(kb + 3, na, nb, nz);
-                uint32_t r[32];
+                if (kb + 3 < nk) USAF_LOAD(kb + 3, na, nz);
                 const int st = g % kStages;
+                const int kh0 = kb * kBK + hf * 32;   // first K index of this lane's half-block
+                uint32_t szr[32];
                 if (TRANS) {
-                    // this k-block's 64 per-row (scale|zero) words arrive with the stage's TMA
+                    // this k-block's per-row (scale|zero) words arrive with the stage's TMA
                     if (!mbar_wait(&S.full_b[st], (g / kStages) & 1, abort_flag, err)) { ok = false; break; }
-                    const uint32_t *ring = sz_ring + st * kBK;
-                    uint32_t szr[kBK];
+                    const uint32_t *ring = sz_ring + st * kBK + hf * 32;
 #pragma unroll
-                    for (int i = 0; i < kBK / 4; ++i) {
+                    for (int i = 0; i < 8; ++i) {
                         uint4 v4 = *reinterpret_cast<const uint4 *>(ring + 4 * i);
                         szr[4 * i] = v4.x; szr[4 * i + 1] = v4.y; szr[4 * i + 2] = v4.z; szr[4 * i + 3] = v4.w;
                     }
-                    dequant_block_rows(a0, b0, szr, r);
-                } else {
-                    dequant_block(a0, b0, (uint16_t)(z0 & 0xFFFF), (uint16_t)(z0 >> 16), r);
                 }
-                const int k0 = kb * kBK;
-                if (ncol < k0 + kBK) {
-                    // trained coordinates of this lane in this k-block (rare): patch
-                    do {
-                        patch_elem(r, ncol - k0, __bfloat16_as_ushort(__float2bfloat16_rn(nval)));
+                const int rel = qc0 - kh0;
+                const bool hit = rel >= 0 && rel < 32;
+                const int pj = hit ? (rel >> 1) : 0xFF;
+                const uint32_t m2 = qv0 | (qv0 << 16);
+                const uint32_t sel = (rel & 1) ? 0x5410u : 0x3254u;
+                uint32_t r[16];
+                dequant16<TRANS>(a0, z0, szr, pj, m2, sel, r);
+                if (hit) {
+                    // advance the queue; more coordinates in this block take the slow path
+                    ++cur;
+                    qc0 = qc1; qv0 = qv1;
+                    qc1 = 0x7fffffff;
+                    if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
+                    while (qc0 < kh0 + 32) {
+                        patch_elem16(r, qc0 - kh0, qv0);
                         ++cur;
-                        if (cur < cend) { ncol = ov_idx[cur]; nval = ov_val[cur]; }
-                        else ncol = 0x7fffffff;
-                    } while (ncol < k0 + kBK);
+                        qc0 = qc1; qv0 = qv1;
+                        qc1 = 0x7fffffff;
+                        if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
+                    }
                 }
                 if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
                 tc_fence_after();
-                tmem_st_32x32b_x32(tbase + lane_off + kAcol + st * 32, r);
+                tmem_st_32x32b_x16(tbase + lane_off + kAcol + st * 32 + hf * 16, r);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&S.full_a[st]);
-                a0 = a1; b0 = b1; z0 = z1;
-                a1 = a2; b1 = b2; z1 = z2;
-                a2 = na; b2 = nb; z2 = nz;
+                a0 = a1; z0 = z1;
+                a1 = a2; z1 = z2;
+                a2 = na; z2 = nz;
             }
 #undef USAF_LOAD
             if (!ok) break;
-            // ---- epilogue of this tile ----
+            // ---- epilogue of this tile: warp group hf drains 32-column chunks hf, hf+2, ...
             if (!mbar_wait(&S.acc, it & 1, abort_flag, err)) { ok = false; break; }
             tc_fence_after();
-            for (int c0 = 0; c0 < ntok; c0 += 32) {
+            const int gt = row;   // thread index inside the 128-thread group
+            for (int c0 = hf * 32; c0 < ntok; c0 += 64) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + lane_off + c0, v);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    stg[i * kStageLd + t] = __float2bfloat16_rn(__uint_as_float(v[i]));
-                named_bar_sync(1, 128);
+                    stg_g[i * kStageLd + row] = __float2bfloat16_rn(__uint_as_float(v[i]));
+                named_bar_sync(1 + hf, 128);
                 if (MODE == MODE_DOWN || MODE == MODE_GU_BWD) {
                     const int ld = MODE == MODE_DOWN ? R : C;
-                    for (int item = t; item < 32 * 16; item += 128) {
+                    for (int item = gt; item < 32 * 16; item += 128) {
                         const int j = item >> 4, sg = item & 15;
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
                             *reinterpret_cast<uint4 *>(out0 + slot * ld + h0 + sg * 8) =
-                                *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
+                                *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
                         }
                     }
                 } else if (MODE == MODE_GATE_UP) {
                     const int I = R / 2;
-                    for (int item = t; item < 32 * 8; item += 128) {
+                    for (int item = gt; item < 32 * 8; item += 128) {
                         const int j = item >> 3, sg = item & 7;
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
-                            uint4 gv = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
-                            uint4 uv = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + 64 + sg * 8);
+                            uint4 gv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
+                            uint4 uv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + 64 + sg * 8);
                             const __nv_bfloat16 *g8 = reinterpret_cast<const __nv_bfloat16 *>(&gv);
                             const __nv_bfloat16 *u8 = reinterpret_cast<const __nv_bfloat16 *>(&uv);
                             __align__(16) __nv_bfloat16 h8[8];
@@ -434,12 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {  // MODE_DOWN_BWD: SwiGLU backward with the forward's gate/up
                     const int I = C;
-                    for (int item = t; item < 32 * 16; item += 128) {
+                    for (int item = gt; item < 32 * 16; item += 128) {
                         const int j = item >> 4, sg = item & 15;
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
                             const int i0 = h0 + sg * 8;
-                            uint4 dv = *reinterpret_cast<const uint4 *>(stg + j * kStageLd + sg * 8);
+                            uint4 dv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
                             uint4 gv = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * I + i0);
                             uint4 uv = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * I + I + i0);
                             const __nv_bfloat16 *d8 = reinterpret_cast<const __nv_bfloat16 *>(&dv);
@@ -463,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                named_bar_sync(1, 128);
+                named_bar_sync(1 + hf, 128);
             }
             tc_fence_before();
             mbar_arrive(&S.acc_empty);
@@ -546,8 +558,8 @@ bool shape_ok_common(const usaf_qweight *w) {
 
 }  // namespace
 
-bool tc_supported_gate_up(const usaf_qweight *w) { return shape_ok_common(w) && w->R % 128 == 0; }
-bool tc_supported_down(const usaf_qweight *w) { return shape_ok_common(w) && w->R % 128 == 0; }
+bool tc_supported_gate_up(const usaf_qweight *w) { return shape_ok_common(w) && w->qP && w->R % 128 == 0; }
+bool tc_supported_down(const usaf_qweight *w) { return shape_ok_common(w) && w->qP && w->R % 128 == 0; }
 static bool trans_ok(const usaf_qweight *w) {
     return shape_ok_common(w) && w->qT && w->szT && w->C % 128 == 0 && w->group_size % 128 == 0 &&
            (w->n_ov == 0 || (w->colT_ptr && w->rowT && w->valT));

@@ -188,19 +188,25 @@ extern "C" int usaf_quant_int4(const void *x, int32_t x_dtype, int64_t numel, in
 
 // ---- column-major copy for the backward GEMMs ------------------------------
 namespace usaf {
-// qT[(e*C + c)*(R/2) + rp] = code(e, 2rp, c) | code(e, 2rp+1, c) << 4
+// qT: storage column c of expert e, codes along rows r, 8 rows per 32-bit
+// word in the dequant order e0 e2 e4 e6 | e1 e3 e5 e7 (see usaf_int4_repack)
 __global__ void int4_transpose_codes(const uint8_t *__restrict__ q, int E, int R, int C,
-                                     uint8_t *__restrict__ qT) {
-    const int64_t total = (int64_t)E * C * (R / 2);
+                                     uint32_t *__restrict__ qT) {
+    const int64_t total = (int64_t)E * C * (R / 8);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        int64_t rp = i % (R / 2);
-        int64_t ec = i / (R / 2);
+        int64_t r8 = i % (R / 8);
+        int64_t ec = i / (R / 8);
         int64_t c = ec % C, e = ec / C;
-        int64_t f0 = ((e * R + 2 * rp) * C + c), f1 = f0 + C;
-        uint32_t c0 = (q[f0 >> 1] >> ((f0 & 1) * 4)) & 0xF;
-        uint32_t c1 = (q[f1 >> 1] >> ((f1 & 1) * 4)) & 0xF;
-        qT[i] = (uint8_t)(c0 | (c1 << 4));
+        uint32_t out = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            int64_t f = (e * R + r8 * 8 + k) * C + c;
+            uint32_t code = (q[f >> 1] >> ((f & 1) * 4)) & 0xF;
+            int slot = (k & 1) ? 4 + (k >> 1) : (k >> 1);
+            out |= code << (4 * slot);
+        }
+        qT[i] = out;
     }
 }
 // szT[(e*(C/gs) + cb)*R + r] = s[(e*R + r)*(C/gs) + cb] | z[...] << 16
@@ -222,12 +228,46 @@ __global__ void int4_transpose_scales(const uint16_t *__restrict__ s, const uint
 extern "C" int usaf_int4_transpose(const void *q, const void *s, const void *z, int32_t E, int32_t R,
                                    int32_t C, int32_t group_size, void *qT, void *szT, void *stream) {
     USAF_REQUIRE(q && s && z && qT && szT && E >= 1 && R >= 2 && C >= 1 && group_size >= 1);
-    if (R % 2 || C % group_size) return USAF_EUNSUPPORTED;
+    if (R % 8 || C % group_size) return USAF_EUNSUPPORTED;
     cudaStream_t st = as_stream(stream);
     unsigned grid = 148 * 16;
-    int4_transpose_codes<<<grid, 256, 0, st>>>((const uint8_t *)q, E, R, C, (uint8_t *)qT);
+    int4_transpose_codes<<<grid, 256, 0, st>>>((const uint8_t *)q, E, R, C, (uint32_t *)qT);
     int4_transpose_scales<<<grid, 256, 0, st>>>((const uint16_t *)s, (const uint16_t *)z, E, R, C,
                                                 group_size, (uint32_t *)szT);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
+}
+
+// ---- dequant-friendly nibble order for the tensor-core producers ------------
+// Within every 32-bit word (8 consecutive elements e0..e7) the codes are
+// stored as  e0 e2 e4 e6 | e1 e3 e5 e7  (nibble k at bits 4k), so that
+// ((w >> 4i) & 0x000F000F) holds the pair (e_2i, e_2i+1) in the two fp16
+// lanes -- one shift and one LOP3 per pair with the 0x6400 magic number.
+namespace usaf {
+__device__ __forceinline__ uint32_t repack_word(uint32_t w) {
+    uint32_t out = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t byte = (w >> (8 * i)) & 0xFF;      // e_2i (low) | e_2i+1 (high)
+        out |= (byte & 0xF) << (4 * i);
+        out |= (byte >> 4) << (16 + 4 * i);
+    }
+    return out;
+}
+__global__ void int4_repack_words(const uint32_t *__restrict__ in, int64_t nwords,
+                                  uint32_t *__restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nwords;
+         i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = repack_word(in[i]);
+}
+}  // namespace usaf
+
+extern "C" int usaf_int4_repack(const void *q, int64_t numel, void *qp, void *stream) {
+    USAF_REQUIRE(q && qp && numel >= 0);
+    if (numel % 8) return USAF_EUNSUPPORTED;
+    if (numel == 0) return USAF_OK;
+    int4_repack_words<<<148 * 16, 256, 0, as_stream(stream)>>>((const uint32_t *)q, numel / 8,
+                                                                (uint32_t *)qp);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }

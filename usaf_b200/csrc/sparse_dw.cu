@@ -124,8 +124,8 @@ __global__ void __launch_bounds__(kThr) sddmm_kernel(usaf_route_plan pl, usaf_qw
         const int rr = threadIdx.x + h * kThr;
         jb[h] = je[h] = 0;
         if (rr < rows_here) {
-            jb[h] = w.row_ptr[(int64_t)e * R + rb0 + rr];
-            je[h] = w.row_ptr[(int64_t)e * R + rb0 + rr + 1];
+            jb[h] = w.row_ptr[((int64_t)e * R + rb0 + rr) * 2];       // both half segments
+            je[h] = w.row_ptr[((int64_t)e * R + rb0 + rr) * 2 + 2];
         }
     }
     for (int t0 = 0; t0 < cnt; t0 += kTC) {

@@ -92,8 +92,8 @@ class Projection:
         E, R, Cc = (int(x) for x in shape)
         if Cc % group_size != 0:
             raise ValueError("int4 groups must not straddle rows (C % group_size != 0)")
-        if E * R * Cc >= 2 ** 31:
-            raise ValueError("projection too large for 32-bit flat indices")
+        if 2 * E * R * Cc >= 2 ** 32:
+            raise ValueError("projection too large for 32-bit overlay keys")
         self.E, self.R, self.C, self.group_size = E, R, Cc, group_size
         self.shape = (E, R, Cc)
         self.q = q.reshape(-1).contiguous()
@@ -106,9 +106,12 @@ class Projection:
         self.colT_ptr = self.rowT = self.valT = None
         self.csr_to_compact = self.compact_to_csr = self.compact_to_csc = None
         self.scratch = None
-        self.qT = self.szT = None
-        if dtype == torch.bfloat16 and R % 2 == 0:
-            # column-major copy for the tensor-core backward GEMMs (built once)
+        self.qT = self.szT = self.qP = None
+        if dtype == torch.bfloat16 and R % 8 == 0 and Cc % 8 == 0:
+            # dequant-ordered copies for the tensor-core GEMMs (built once):
+            # row-major for the forward, column-major for the backward
+            self.qP = torch.empty_like(self.q)
+            call("usaf_int4_repack", ptr(self.q), E * R * Cc, ptr(self.qP), stream())
             self.qT = torch.empty_like(self.q)
             self.szT = torch.empty(E * (Cc // group_size) * R, dtype=torch.int32, device=self.device)
             call("usaf_int4_transpose", ptr(self.q), ptr(self.s), ptr(self.z), E, R, Cc, group_size,
@@ -125,22 +128,26 @@ class Projection:
         self.n_ov = n
         E, R, Cc = self.E, self.R, self.C
         ar = torch.arange(n, device=dev, dtype=torch.int64)
-        # CSR: ascending flat index
-        kcsr, pcsr = sort_u32(idx, ar)
-        flat = kcsr.to(torch.int64)
-        self.row_ptr = build_rowptr(flat // Cc, E * R)
-        self.col = _i32(flat % Cc)
-        self.csr_to_compact = _i32(pcsr)
-        self.compact_to_csr = torch.empty(n, dtype=torch.int32, device=dev)
-        self.compact_to_csr[pcsr] = torch.arange(n, device=dev, dtype=torch.int32)
-        # CSC: ascending (e, c, r)
+        M32 = 0xFFFFFFFF
         e = idx // (R * Cc)
         r = (idx // Cc) % R
         c = idx % Cc
-        key = (e * Cc + c) * R + r
-        kcsc, pcsc = sort_u32(key, ar)
-        kc = kcsc.to(torch.int64)
-        self.colT_ptr = build_rowptr(kc // R, E * Cc)
+        # CSR: segments (row, half) with half = (col / 32) % 2, ascending col inside:
+        # the tensor-core producers split every 64-wide k-block between two
+        # threads per row, each walking its own sorted segment
+        key = ((e * R + r) * 2 + ((c >> 5) & 1)) * Cc + c
+        kcsr, pcsr = sort_u32(key, ar)
+        k64 = kcsr.to(torch.int64) & M32
+        self.row_ptr = build_rowptr(k64 // Cc, E * R * 2)
+        self.col = _i32(k64 % Cc)
+        self.csr_to_compact = _i32(pcsr)
+        self.compact_to_csr = torch.empty(n, dtype=torch.int32, device=dev)
+        self.compact_to_csr[pcsr] = torch.arange(n, device=dev, dtype=torch.int32)
+        # CSC: segments (column, half) with half = (row / 32) % 2, ascending row
+        keyT = ((e * Cc + c) * 2 + ((r >> 5) & 1)) * R + r
+        kcsc, pcsc = sort_u32(keyT, ar)
+        kc = kcsc.to(torch.int64) & M32
+        self.colT_ptr = build_rowptr(kc // R, E * Cc * 2)
         self.rowT = _i32(kc % R)
         self.compact_to_csc = torch.empty(n, dtype=torch.int32, device=dev)
         self.compact_to_csc[pcsc] = torch.arange(n, device=dev, dtype=torch.int32)
@@ -165,7 +172,7 @@ class Projection:
             if self.n_ov:
                 st.row_ptr, st.col, st.val = ptr(self.row_ptr), ptr(self.col), ptr(self.val)
                 st.colT_ptr, st.rowT, st.valT = ptr(self.colT_ptr), ptr(self.rowT), ptr(self.valT)
-            st.qT, st.szT = ptr(self.qT), ptr(self.szT)
+            st.qT, st.szT, st.qP = ptr(self.qT), ptr(self.szT), ptr(self.qP)
             self._struct = st
         return self._struct
 
