@@ -37,7 +37,7 @@ constexpr int kMaxTok = kSub * kMaxSub;          // 384 tokens per CTA
 constexpr int kSubBytes = kSub * kBK * 2;        // 16 KB per TMA box
 constexpr int kStageBytes = kMaxSub * kSubBytes; // 48 KB per stage
 constexpr int kAcol = kMaxTok;                   // first TMEM column of the A stages
-constexpr int kThreads = 384;                   // 0 TMA, 1 MMA, 4-11 dequant + epilogue
+constexpr int kThreads = 512;  // warps 0-3 epilogue, 4 TMA, 5 MMA (+TMEM alloc), 8-15 dequant
 constexpr int kStageLd = 136;                    // epilogue staging row stride (elements)
 
 enum : int { MODE_GATE_UP = 0, MODE_DOWN = 1, MODE_DOWN_BWD = 2, MODE_GU_BWD = 3 };
@@ -54,7 +54,7 @@ struct alignas(8) TcShared {
     int abort_flag;
 };
 
-constexpr size_t kStgBytes = (size_t)2 * 32 * kStageLd * 2;  // epilogue staging, one per warp group
+constexpr size_t kStgBytes = (size_t)32 * kStageLd * 2;  // epilogue staging tile
 constexpr size_t kSzBytes = (size_t)4 * kBK * 4;          // transposed-mode scale ring
 // stages + epilogue staging + scale ring + shared block + tile prefix / counts (E <= 1024)
 constexpr size_t kSmemBytes =
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int c4[4], n4[4], mine = 0;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            int e_ = tid * 4 + q;   // 384 threads x 4 >= 1024 experts
+            int e_ = tid * 4 + q;   // 512 threads x 4 >= 1024 experts
             c4[q] = e_ < E ? pl.expert_cnt[e_] : 0;
             n4[q] = (c4[q] + kMaxTok - 1) / kMaxTok;
             mine += n4[q];
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_init(&S.empty[st], 1);
             }
             mbar_init(&S.acc, 1);
-            mbar_init(&S.acc_empty, 256);
+            mbar_init(&S.acc_empty, 128);
             fence_barrier_init();
         }
     }
@@ -216,12 +216,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if ((int)blockIdx.x >= n_work) return;  // whole CTA leaves before any TMEM / async work
     volatile int *abort_flag = &S.abort_flag;
 
-    if (warp == 1) tmem_alloc(&S.tmem_base, 512);
+    if (warp == 5) tmem_alloc(&S.tmem_base, 512);
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = S.tmem_base;
 
-    if (warp == 0) {
+    if (warp == 4) {
         // ---------------- TMA producer (token rows, 32-row boxes) ----------------
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     drain_wait(&S.full_b[gg % kStages], (gg / kStages) & 1, err);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 5) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             int g = 0, it = 0;
@@ -288,25 +288,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mma_commit(&S.acc);
             }
         }
-    } else if (warp >= 4) {
-        // ---------------- dequant producers + epilogue ----------------
-        // 8 warps: warp w owns TMEM lane quarter w%4 and K half hf of every
-        // 64-wide k-block (columns [hf*32, hf*32+32))
-        const int t = tid - 128;                // 0..255
+    } else if (warp >= 8) {
+        // ---------------- dequant producers (warps 8-15) ----------------
+        // warp w owns TMEM lane quarter w%4 and K half hf of every 64-wide
+        // k-block (columns [hf*32, hf*32+32))
+        const int t = tid - 256;                // 0..255
         const int row = t & 127;                // TMEM lane = weight row of the tile
         const int hf = t >> 7;
         const uint32_t lane_off = ((uint32_t)(warp & 3) * 32) << 16;
         const int gs = w.group_size;
         const unsigned short *s_ptr = reinterpret_cast<const unsigned short *>(w.s);
         const unsigned short *z_ptr = reinterpret_cast<const unsigned short *>(w.z);
-        __nv_bfloat16 *stg_g = stg + hf * 32 * kStageLd;   // this group's staging tile
         int g = 0, it = 0;
         bool ok = true;
         for (int work = blockIdx.x; work < n_work && ok; work += gridDim.x, ++it) {
             int e, t0, ntok;
             decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
             const int rb = work % nrb;
-            const int row0 = pl.expert_off[e] + t0;
             int64_t crow;        // row of q (fwd) or qT (bwd) this lane dequantizes
             int j0 = 0, h0 = 0;  // output column base
             if (MODE == MODE_GATE_UP) {
@@ -334,7 +332,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (cur < cend) { qc0 = ov_idx[cur]; qv0 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur])); }
                 if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
             }
-            // rolling 3-deep prefetch ring of (codes, scale|zero)
+            // 3-slot prefetch ring: slot i holds k-block kb with kb % 3 == i; a slot
+            // is refilled with kb+3 right after it is consumed (no register moves
+            // of in-flight loads, which would wait for them)
             uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, a2 = a0;
             uint32_t z0 = 0, z1 = 0, z2 = 0;
 #define USAF_LOAD(kb_, A_, Z_)                                                                   \
@@ -348,16 +348,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             USAF_LOAD(0, a0, z0);
             if (1 < nk) USAF_LOAD(1, a1, z1);
             if (2 < nk) USAF_LOAD(2, a2, z2);
-            for (int kb = 0; kb < nk; ++kb, ++g) {
-                uint4 na = a2;
-                uint32_t nz = z2;
-                if (kb + 3 < nk) USAF_LOAD(kb + 3, na, nz);
+            auto kstep = [&](int kb, uint4 &A, uint32_t &Z) {
                 const int st = g % kStages;
                 const int kh0 = kb * kBK + hf * 32;   // first K index of this lane's half-block
                 uint32_t szr[32];
                 if (TRANS) {
                     // this k-block's per-row (scale|zero) words arrive with the stage's TMA
-                    if (!mbar_wait(&S.full_b[st], (g / kStages) & 1, abort_flag, err)) { ok = false; break; }
+                    if (!mbar_wait(&S.full_b[st], (g / kStages) & 1, abort_flag, err)) { ok = false; return; }
                     const uint32_t *ring = sz_ring + st * kBK + hf * 32;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -371,7 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t m2 = qv0 | (qv0 << 16);
                 const uint32_t sel = (rel & 1) ? 0x5410u : 0x3254u;
                 uint32_t r[16];
-                dequant16<TRANS>(a0, z0, szr, pj, m2, sel, r);
+                dequant16<TRANS>(A, Z, szr, pj, m2, sel, r);
+                if (kb + 3 < nk) USAF_LOAD(kb + 3, A, Z);   // refill the consumed slot
                 if (hit) {
                     // advance the queue; more coordinates in this block take the slow path
                     ++cur;
@@ -386,30 +384,63 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
                     }
                 }
-                if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
+                if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) { ok = false; return; }
                 tc_fence_after();
                 tmem_st_32x32b_x16(tbase + lane_off + kAcol + st * 32 + hf * 16, r);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&S.full_a[st]);
-                a0 = a1; z0 = z1;
-                a1 = a2; z1 = z2;
-                a2 = na; z2 = nz;
+                ++g;
+            };
+            for (int kb = 0; kb < nk && ok; kb += 3) {
+                kstep(kb, a0, z0);
+                if (kb + 1 < nk && ok) kstep(kb + 1, a1, z1);
+                if (kb + 2 < nk && ok) kstep(kb + 2, a2, z2);
             }
 #undef USAF_LOAD
             if (!ok) break;
-            // ---- epilogue of this tile: warp group hf drains 32-column chunks hf, hf+2, ...
-            if (!mbar_wait(&S.acc, it & 1, abort_flag, err)) { ok = false; break; }
+        }
+    } else if (warp < 4) {
+        // ---------------- epilogue (warps 0-3): overlaps the next tile's dequant ----------------
+        const int row = tid;                       // TMEM lane
+        const uint32_t lane_off = ((uint32_t)warp * 32) << 16;
+        int it = 0;
+        for (int work = blockIdx.x; work < n_work; work += gridDim.x, ++it) {
+            int e, t0, ntok;
+            decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+            const int rb = work % nrb;
+            const int row0 = pl.expert_off[e] + t0;
+            int j0 = 0, h0 = 0;
+            if (MODE == MODE_GATE_UP) j0 = rb * 64;
+            else h0 = rb * 128;
+            if (!mbar_wait(&S.acc, it & 1, abort_flag, err)) break;
             tc_fence_after();
-            const int gt = row;   // thread index inside the 128-thread group
-            for (int c0 = hf * 32; c0 < ntok; c0 += 64) {
+            const int gt = row;
+            __nv_bfloat16 *stg_g = stg;
+            for (int c0 = 0; c0 < ntok; c0 += 32) {
+                // MODE_DOWN_BWD: this thread's forward gate/up vectors for the chunk
+                // (items gt + 128 q: token j = gt/16 + 8 q, column group gt%16), loaded
+                // before the TMEM drain so their latency overlaps it
+                uint4 gpre[4], upre[4];
+                if (MODE == MODE_DOWN_BWD) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int j = (gt >> 4) + 8 * q;
+                        if (c0 + j < ntok) {
+                            const int64_t slot = row0 + c0 + j;
+                            const int i0 = h0 + (gt & 15) * 8;
+                            gpre[q] = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * C + i0);
+                            upre[q] = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * C + C + i0);
+                        }
+                    }
+                }
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(tbase + lane_off + c0, v);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
                     stg_g[i * kStageLd + row] = __float2bfloat16_rn(__uint_as_float(v[i]));
-                named_bar_sync(1 + hf, 128);
+                named_bar_sync(1, 128);
                 if (MODE == MODE_DOWN || MODE == MODE_GU_BWD) {
                     const int ld = MODE == MODE_DOWN ? R : C;
                     for (int item = gt; item < 32 * 16; item += 128) {
@@ -446,14 +477,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {  // MODE_DOWN_BWD: SwiGLU backward with the forward's gate/up
                     const int I = C;
-                    for (int item = gt; item < 32 * 16; item += 128) {
-                        const int j = item >> 4, sg = item & 15;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int j = (gt >> 4) + 8 * q, sg = gt & 15;
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
                             const int i0 = h0 + sg * 8;
                             uint4 dv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
-                            uint4 gv = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * I + i0);
-                            uint4 uv = *reinterpret_cast<const uint4 *>(in1 + slot * 2 * I + I + i0);
+                            const uint4 gv = gpre[q], uv = upre[q];
                             const __nv_bfloat16 *d8 = reinterpret_cast<const __nv_bfloat16 *>(&dv);
                             const __nv_bfloat16 *g8 = reinterpret_cast<const __nv_bfloat16 *>(&gv);
                             const __nv_bfloat16 *u8 = reinterpret_cast<const __nv_bfloat16 *>(&uv);
@@ -462,11 +493,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int q = 0; q < 8; ++q) {
                                 float dh = __bfloat162float(d8[q]);
                                 float gf = __bfloat162float(g8[q]), uf = __bfloat162float(u8[q]);
-                                float sg_ = __bfloat162float(__float2bfloat16_rn(
-                                    __fdiv_rn(gf, __fadd_rn(1.0f, expf(-gf)))));
+                                const float den = __fadd_rn(1.0f, expf(-gf));
+                                float sg_ = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(gf, den)));
                                 float ds = __bfloat162float(__float2bfloat16_rn(__fmul_rn(dh, uf)));
                                 du8[q] = __float2bfloat16_rn(__fmul_rn(dh, sg_));
-                                float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gf)));
+                                float sig = __frcp_rn(den);   // 1/den, correctly rounded like 1.0f/den
                                 float tt = __fadd_rn(1.0f, __fmul_rn(gf, __fsub_rn(1.0f, sig)));
                                 dg8[q] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(ds, sig), tt));
                             }
@@ -475,16 +506,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
-                named_bar_sync(1 + hf, 128);
+                named_bar_sync(1, 128);
             }
             tc_fence_before();
             mbar_arrive(&S.acc_empty);
         }
-        if (!ok) drain_wait(&S.acc, it & 1, err);  // MMAs of an aborted tile finish before dealloc
+        // accumulators of a tile whose epilogue was skipped must be complete before dealloc
+        if (*abort_flag) drain_wait(&S.acc, it & 1, err);
         tc_fence_before();
     }
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 5) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
     }
