@@ -86,6 +86,10 @@ typedef struct {
     const int8_t   *qT;
     const uint32_t *szT;
     const int8_t   *qP;
+    /* overlay bitmap [E*R*C/32]: bit (c % 32) of word (e*R + r)*(C/32) + c/32
+     * is set for every overlay coordinate (e, r, c).  Optional (NULL selects
+     * the SIMT gradient kernel); the tensor-core usaf_sparse_dw reads it. */
+    const uint32_t *ov_mask;
 } usaf_qweight;
 
 /* ---- int4 format ---------------------------------------------------------

@@ -32,7 +32,8 @@ class QWeight(C.Structure):
     _fields_ = [("E", I32), ("R", I32), ("C", I32), ("group_size", I32),
                 ("q", P), ("s", P), ("z", P), ("n_ov", I32),
                 ("row_ptr", P), ("col", P), ("val", P),
-                ("colT_ptr", P), ("rowT", P), ("valT", P), ("qT", P), ("szT", P), ("qP", P)]
+                ("colT_ptr", P), ("rowT", P), ("valT", P), ("qT", P), ("szT", P), ("qP", P),
+                ("ov_mask", P)]
 
 
 # name -> (restype, argtypes)

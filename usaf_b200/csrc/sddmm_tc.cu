@@ -1,0 +1,399 @@
+// Expert-weight gradients on tcgen05 (bf16 activations).
+//
+// For expert e the weight gradient is the product over its routed slots
+//   D_e[r][c] = sum_{s in slots of e} gout[s][r] * gin[s][c]
+// (gout = dgu / dcur [P, R], gin = x_perm / h [P, C], both slot-major).  The
+// reference forms D_e densely (F.linear backward, usaf/qwen3moe_dml.py:43-56)
+// and keeps only the selected coordinates (usaf/moe_loader.py:564-578).  Here
+// D_e is formed tile by tile in TMEM and never written out: the epilogue
+// keeps what the caller needs.
+//   EPI_SPARSE   : the selected coordinates, read from the overlay bitmap, as
+//                  dtype(D) into a CSR-ordered fp32 vector; a second kernel
+//                  adds scale * that value to the compact gradient.
+//   EPI_DENSE_ABS: |dtype(D)| at every coordinate (importance pass,
+//                  usaf/importance.py).
+//
+// Tile = 128 storage rows x 256 columns, K = the expert's slots in blocks of
+// 64.  Both operands reach shared memory as TMA boxes of 64 slots x 64
+// rows/columns with the 128-byte swizzle; for the MMA they are MN-major
+// (rows r / columns c contiguous, slots along K), so no transpose is needed.
+// Slots of the next expert that fall inside the last 64-slot block are
+// zeroed in shared memory before the MMA reads it.
+//
+// Persistent CTAs (one per SM) walk work items (expert, 128-row block); an
+// item runs its column tiles back to back.  Warp 0 issues TMA, warp 1 the
+// MMAs (and owns TMEM), warps 2-5 drain the accumulators; TMEM holds two
+// 256-column accumulators so the drain of one tile overlaps the MMAs of
+// the next.
+#include <cudaTypedefs.h>
+
+#include "tc_common.cuh"
+
+namespace usaf {
+using namespace tc;
+
+namespace {
+
+constexpr int kSM = 128;                 // storage rows per tile (MMA M)
+constexpr int kSN = 256;                 // columns per tile (MMA N)
+constexpr int kSK = 64;                  // slots per k-block
+constexpr int kSStages = 4;
+constexpr int kSThreads = 192;
+constexpr int kBox = kSK * 64 * 2;       // one TMA box: 64 slots x 64 bf16 = 8 KB
+constexpr int kAStage = 2 * kBox;        // 128 rows
+constexpr int kStage = kAStage + 4 * kBox;   // + 256 columns = 48 KB
+constexpr int kRowLd = 33;               // epilogue per-thread row (floats)
+
+enum : int { EPI_SPARSE = 0, EPI_DENSE_ABS = 1 };
+
+struct alignas(8) SShared {
+    uint64_t full[kSStages];
+    uint64_t empty[kSStages];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t mma_done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+constexpr size_t kSSmem = (size_t)kSStages * kStage + (size_t)128 * kRowLd * 4 + sizeof(SShared) + 1024;
+
+__device__ __forceinline__ void s_drain(uint64_t *bar, uint32_t parity, int *err) {
+    uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > kWaitBudgetNs) {
+            atomicOr(err, USAF_ERR_WAIT_TIMEOUT);
+            return;
+        }
+    }
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// MN-major operand with the 128-byte swizzle: 64-element MN blocks LBO = 8 KB
+// apart (one TMA box each), 8-slot groups SBO = 1 KB apart, version 1 (sm_100)
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(kBox >> 4) << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// bf16 x bf16 -> fp32, A and B MN-major (transpose bits 15 and 16)
+__host__ __device__ constexpr uint32_t idesc_mn(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ float round_bf16(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kSThreads, 1)
+    sddmm_tc_kernel(const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_in,
+                    usaf_route_plan pl, int R, int C, const int32_t *__restrict__ row_ptr,
+                    const uint32_t *__restrict__ mask, float *__restrict__ out) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *sb = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    float *rows_s = reinterpret_cast<float *>(sb + (size_t)kSStages * kStage);
+    SShared &S = *reinterpret_cast<SShared *>(sb + (size_t)kSStages * kStage + (size_t)128 * kRowLd * 4);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int E = pl.E;
+    const int nrb = R / kSM;
+    const int ncb = (C + kSN - 1) / kSN;
+    const int n_items = E * nrb;
+    int *err = pl.err;
+    if (tid == 0) {
+        S.abort_flag = 0;
+        for (int s = 0; s < kSStages; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&S.acc_full[b], 1);
+            mbar_init(&S.acc_empty[b], 128);
+        }
+        mbar_init(&S.mma_done, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    volatile int *abort_flag = &S.abort_flag;
+    if (warp == 1) tmem_alloc(&S.tmem_base, 512);
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = S.tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            prefetch_tmap(&tm_out);
+            prefetch_tmap(&tm_in);
+            int g = 0, last_g = -1;
+            for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+                const int e = item / nrb, rb = item % nrb;
+                const int cnt = pl.expert_cnt[e];
+                if (cnt == 0) continue;
+                const int row0 = pl.expert_off[e];
+                const int nk = (cnt + kSK - 1) / kSK;
+                bool ok = true;
+                for (int cb = 0; cb < ncb && ok; ++cb) {
+                    const int c0 = cb * kSN;
+                    const int nb = min(4, (C - c0) / 64);
+                    for (int kb = 0; kb < nk; ++kb, ++g) {
+                        const int st = g % kSStages;
+                        if (!mbar_wait(&S.empty[st], ((g / kSStages) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&S.full[st], (uint32_t)((2 + nb) * kBox));
+                        unsigned char *dst = sb + (size_t)st * kStage;
+                        const int y = row0 + kb * kSK;
+                        tma_load_2d(dst, &tm_out, &S.full[st], rb * kSM, y);
+                        tma_load_2d(dst + kBox, &tm_out, &S.full[st], rb * kSM + 64, y);
+                        for (int j = 0; j < nb; ++j)
+                            tma_load_2d(dst + kAStage + j * kBox, &tm_in, &S.full[st], c0 + 64 * j, y);
+                        last_g = g;
+                    }
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag)
+                for (int gg = max(0, last_g - kSStages + 1); gg <= last_g; ++gg)
+                    s_drain(&S.full[gg % kSStages], (gg / kSStages) & 1, err);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (lane 0) + tail zeroing (whole warp) ----------------
+        int g = 0, it = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+            const int e = item / nrb;
+            const int cnt = pl.expert_cnt[e];
+            if (cnt == 0) continue;
+            const int nk = (cnt + kSK - 1) / kSK;
+            for (int cb = 0; cb < ncb && ok; ++cb, ++it) {
+                const int c0 = cb * kSN;
+                const int nb = min(4, (C - c0) / 64);
+                const uint32_t idesc = idesc_mn(kSM, nb * 64);
+                const int buf = it & 1;
+                ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err);
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                tc_fence_after();
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int st = g % kSStages;
+                    ok = mbar_wait(&S.full[st], (g / kSStages) & 1, abort_flag, err);
+                    ok = __all_sync(0xffffffffu, ok);
+                    if (!ok) break;
+                    unsigned char *stage = sb + (size_t)st * kStage;
+                    const int rem = min(kSK, cnt - kb * kSK);
+                    if (rem < kSK) {
+                        // slots [rem, 64) of this block belong to the next expert (or lie
+                        // past the routed slots): zero them in every box of the stage
+                        const int nbox = 2 + nb;
+                        const int per_box = (kSK - rem) * 8;          // 16-byte chunks
+                        for (int i = lane; i < nbox * per_box; i += 32) {
+                            const int bx = i / per_box, k = i % per_box;
+                            *reinterpret_cast<uint4 *>(stage + bx * kBox + rem * 128 + k * 16) =
+                                make_uint4(0, 0, 0, 0);
+                        }
+                        fence_proxy_async();
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        tc_fence_after();
+                        const uint32_t a_s = smem_u32(stage), b_s = a_s + kAStage;
+                        const int nks = (rem + 15) / 16;
+                        for (int kk = 0; kk < nks; ++kk)
+                            mma_ss(tbase + buf * kSN, desc_mn_sw128(a_s + kk * 2048),
+                                   desc_mn_sw128(b_s + kk * 2048), idesc, (kb | kk) != 0);
+                        mma_commit(&S.empty[st]);
+                    }
+                    __syncwarp();
+                }
+                if (!ok) break;
+                if (lane == 0) mma_commit(&S.acc_full[buf]);
+            }
+        }
+        // every MMA this CTA issued has completed before TMEM is released
+        if (lane == 0) {
+            mma_commit(&S.mma_done);
+            s_drain(&S.mma_done, 0, err);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (warps 2-5) ----------------
+        const int q = warp & 3;                      // TMEM lane quarter
+        const int rr = q * 32 + lane;                // row inside the tile
+        const uint32_t lane_off = ((uint32_t)(q * 32)) << 16;
+        float *my_row = rows_s + (q * 32 + lane) * kRowLd;
+        const int cw = C / 32;                       // bitmap words per storage row
+        int it = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            const int e = item / nrb, rb = item % nrb;
+            const int cnt = pl.expert_cnt[e];
+            const int64_t grow = (int64_t)e * R + rb * kSM + rr;   // global storage row
+            int p0 = 0, p1 = 0;
+            if (EPI == EPI_SPARSE) {
+                p0 = row_ptr[grow * 2];
+                p1 = row_ptr[grow * 2 + 1];
+            }
+            if (cnt == 0) {
+                // no slots: the gradient is exactly zero
+                if (EPI == EPI_SPARSE) {
+                    const int pend = row_ptr[grow * 2 + 2];
+                    for (int p = p0; p < pend; ++p) out[p] = 0.0f;
+                } else {
+                    float4 *o = reinterpret_cast<float4 *>(out + grow * C);
+                    for (int i = 0; i < C / 4; ++i) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                continue;
+            }
+            bool ok = true;
+            for (int cb = 0; cb < ncb; ++cb, ++it) {
+                const int c0 = cb * kSN;
+                const int nch = min(8, (C - c0) / 32);
+                uint32_t mw[8];
+                if (EPI == EPI_SPARSE) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) mw[j] = j < nch ? mask[grow * cw + c0 / 32 + j] : 0u;
+                }
+                const int buf = it & 1;
+                if (!mbar_wait(&S.acc_full[buf], (it >> 1) & 1, abort_flag, err)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (j >= nch) break;
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tbase + lane_off + buf * kSN + j * 32, v);
+                    tmem_wait_ld();
+                    if (EPI == EPI_SPARSE) {
+                        uint32_t m = mw[j];
+                        if (m) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) my_row[i] = __uint_as_float(v[i]);
+                            // chunk j holds columns with (c/32) % 2 == j % 2: CSR half j&1
+                            int p = (j & 1) ? p1 : p0;
+                            while (m) {
+                                const int b = __ffs(m) - 1;
+                                m &= m - 1;
+                                out[p++] = round_bf16(my_row[b]);
+                            }
+                            if (j & 1) p1 = p; else p0 = p;
+                        }
+                    } else {
+                        float4 *o = reinterpret_cast<float4 *>(out + grow * C + c0 + j * 32);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            o[i] = make_float4(fabsf(round_bf16(__uint_as_float(v[4 * i]))),
+                                               fabsf(round_bf16(__uint_as_float(v[4 * i + 1]))),
+                                               fabsf(round_bf16(__uint_as_float(v[4 * i + 2]))),
+                                               fabsf(round_bf16(__uint_as_float(v[4 * i + 3]))));
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&S.acc_empty[buf]);
+            }
+            if (!ok) break;
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// compact[c2c[j]] += scale * g[j]   (g already rounded to the activation dtype)
+__global__ void sddmm_accumulate(int n, const float *__restrict__ g, const int32_t *__restrict__ c2c,
+                                 float scale, float *__restrict__ compact) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+        const int pos = c2c[j];
+        compact[pos] = __fadd_rn(compact[pos], __fmul_rn(scale, g[j]));
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 s_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// slot-major bf16 matrix [rows, cols] -> boxes of 64 slots x 64 columns, 128-byte swizzle
+bool s_tmap(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols) {
+    auto fn = s_encode();
+    if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || (cols * 2) % 16) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * 2)};
+    cuuint32_t box[2] = {64u, (cuuint32_t)kSK};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int s_num_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+template <int EPI>
+int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
+                    const __nv_bfloat16 *gin, const int32_t *row_ptr, const uint32_t *mask, float *out,
+                    cudaStream_t st) {
+    CUtensorMap ta, tb;
+    if (!s_tmap(&ta, gout, pl->P_cap, R) || !s_tmap(&tb, gin, pl->P_cap, C)) return USAF_EUNSUPPORTED;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(sddmm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSSmem) != cudaSuccess)
+            return USAF_ECUDA;
+        attr = true;
+    }
+    const int n_items = pl->E * (R / kSM);
+    dim3 grid(std::min(s_num_sms(), n_items));
+    sddmm_tc_kernel<EPI><<<grid, kSThreads, kSSmem, st>>>(ta, tb, *pl, R, C, row_ptr, mask, out);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
+}
+
+}  // namespace
+
+bool sddmm_tc_supported(int R, int C) {
+    return R % kSM == 0 && C % 128 == 0 && s_encode() != nullptr;
+}
+
+// g[j] (CSR order) = bf16(D[e][r][c]) for every overlay entry, then
+// compact[c2c[j]] += scale * g[j]
+int sddmm_tc_sparse(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *gout,
+                    const __nv_bfloat16 *gin, const int32_t *c2c, float scale, float *compact,
+                    float *scratch, cudaStream_t st) {
+    int rc = sddmm_tc_launch<EPI_SPARSE>(pl, w->R, w->C, gout, gin, w->row_ptr, w->ov_mask, scratch, st);
+    if (rc != USAF_OK) return rc;
+    const int n = w->n_ov;
+    sddmm_accumulate<<<std::min((n + 255) / 256, 148 * 16), 256, 0, st>>>(n, scratch, c2c, scale, compact);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
+}
+
+int sddmm_tc_dense_abs(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
+                       const __nv_bfloat16 *gin, float *out, cudaStream_t st) {
+    return sddmm_tc_launch<EPI_DENSE_ABS>(pl, R, C, gout, gin, nullptr, nullptr, out, st);
+}
+
+}  // namespace usaf

@@ -219,6 +219,13 @@ static int sddmm_launch(const usaf_route_plan *pl, const usaf_qweight *w, const 
     return USAF_OK;
 }
 
+bool sddmm_tc_supported(int R, int C);
+int sddmm_tc_sparse(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *gout,
+                    const __nv_bfloat16 *gin, const int32_t *c2c, float scale, float *compact,
+                    float *scratch, cudaStream_t st);
+int sddmm_tc_dense_abs(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
+                       const __nv_bfloat16 *gin, float *out, cudaStream_t st);
+
 }  // namespace usaf
 
 using namespace usaf;
@@ -230,6 +237,9 @@ extern "C" int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w
     if (w->n_ov == 0) return USAF_OK;
     USAF_REQUIRE(csr_to_compact && compact && scratch && w->row_ptr && w->col);
     cudaStream_t st = as_stream(stream);
+    if (dtype == USAF_BF16 && w->ov_mask && sddmm_tc_supported(w->R, w->C))
+        return sddmm_tc_sparse(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin,
+                               csr_to_compact, scale, compact, scratch, st);
     switch (dtype) {
         case USAF_F32: return sddmm_launch<float>(plan, w, (const float *)gout, (const float *)gin, csr_to_compact, scale, compact, scratch, st);
         case USAF_BF16: return sddmm_launch<__nv_bfloat16>(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin, csr_to_compact, scale, compact, scratch, st);
@@ -242,6 +252,8 @@ extern "C" int usaf_expert_dense_dw(const usaf_route_plan *plan, int32_t R, int3
                                     void *stream) {
     USAF_REQUIRE(plan && gout && gin && out && R >= 1 && C >= 1);
     cudaStream_t st = as_stream(stream);
+    if (dtype == USAF_BF16 && sddmm_tc_supported(R, C))
+        return sddmm_tc_dense_abs(plan, R, C, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin, out, st);
     dim3 grid(cdiv(C, 64), cdiv(R, 64), plan->E);
     switch (dtype) {
         case USAF_F32: dense_dw_kernel<float><<<grid, 256, 0, st>>>(*plan, R, C, (const float *)gout, (const float *)gin, out); break;

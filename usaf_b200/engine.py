@@ -106,6 +106,7 @@ class Projection:
         self.colT_ptr = self.rowT = self.valT = None
         self.csr_to_compact = self.compact_to_csr = self.compact_to_csc = None
         self.scratch = None
+        self.ov_mask = None
         self.qT = self.szT = self.qP = None
         if dtype == torch.bfloat16 and R % 8 == 0 and Cc % 8 == 0:
             # dequant-ordered copies for the tensor-core GEMMs (built once):
@@ -152,6 +153,15 @@ class Projection:
         self.compact_to_csc = torch.empty(n, dtype=torch.int32, device=dev)
         self.compact_to_csc[pcsc] = torch.arange(n, device=dev, dtype=torch.int32)
         self._csc_to_compact = pcsc
+        # bitmap of the selected coordinates, one 32-bit word per (row, 32 columns):
+        # the tensor-core gradient epilogue reads a tile's selection from it
+        self.ov_mask = None
+        if Cc % 32 == 0:
+            words = (e * R + r) * (Cc // 32) + (c >> 5)
+            m = torch.zeros(E * R * (Cc // 32), dtype=torch.int64, device=dev)
+            m.index_add_(0, words, torch.ones_like(c) << (c & 31))   # distinct bits: add == or
+            self.ov_mask = torch.where(m >= 2 ** 31, m - 2 ** 32, m).to(torch.int32)
+            del m, words
         self.val = torch.empty(n, dtype=torch.float32, device=dev)
         self.valT = torch.empty(n, dtype=torch.float32, device=dev)
         self.update_overlay_values(master)
@@ -173,6 +183,7 @@ class Projection:
                 st.row_ptr, st.col, st.val = ptr(self.row_ptr), ptr(self.col), ptr(self.val)
                 st.colT_ptr, st.rowT, st.valT = ptr(self.colT_ptr), ptr(self.rowT), ptr(self.valT)
             st.qT, st.szT, st.qP = ptr(self.qT), ptr(self.szT), ptr(self.qP)
+            st.ov_mask = ptr(self.ov_mask) if (self.n_ov and self.ov_mask is not None) else None
             self._struct = st
         return self._struct
 
