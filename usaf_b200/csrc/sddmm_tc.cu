@@ -17,14 +17,15 @@
 // 64.  Both operands reach shared memory as TMA boxes of 64 slots x 64
 // rows/columns with the 128-byte swizzle; for the MMA they are MN-major
 // (rows r / columns c contiguous, slots along K), so no transpose is needed.
-// Slots of the next expert that fall inside the last 64-slot block are
-// zeroed in shared memory before the MMA reads it.
+// Slots of the next expert that fall inside the last 16-slot group the MMA
+// reads are zeroed in shared memory before it does.
 //
 // Persistent CTAs (one per SM) walk work items (expert, 128-row block); an
 // item runs its column tiles back to back.  Warp 0 issues TMA, warp 1 the
-// MMAs (and owns TMEM), warps 2-5 drain the accumulators; TMEM holds two
-// 256-column accumulators so the drain of one tile overlaps the MMAs of
-// the next.
+// MMAs (and owns TMEM), warps 2-5 drain the accumulators, warp 6 passes each
+// filled stage on to the MMA after zeroing the ragged tail of an expert's
+// last k-block; TMEM holds two 256-column
+// accumulators so the drain of one tile overlaps the MMAs of the next.
 #include <cudaTypedefs.h>
 
 #include "tc_common.cuh"
@@ -38,7 +39,7 @@ constexpr int kSM = 128;                 // storage rows per tile (MMA M)
 constexpr int kSN = 256;                 // columns per tile (MMA N)
 constexpr int kSK = 64;                  // slots per k-block
 constexpr int kSStages = 4;
-constexpr int kSThreads = 192;
+constexpr int kSThreads = 224;
 constexpr int kBox = kSK * 64 * 2;       // one TMA box: 64 slots x 64 bf16 = 8 KB
 constexpr int kAStage = 2 * kBox;        // 128 rows
 constexpr int kStage = kAStage + 4 * kBox;   // + 256 columns = 48 KB
@@ -51,6 +52,7 @@ struct alignas(8) SShared {
     uint64_t empty[kSStages];
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
+    uint64_t fixed[kSStages];
     uint64_t mma_done;
     uint32_t tmem_base;
     int abort_flag;
@@ -115,6 +117,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
         for (int s = 0; s < kSStages; ++s) {
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], 1);
+            mbar_init(&S.fixed[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
@@ -166,65 +169,90 @@ __global__ void __launch_bounds__(kSThreads, 1)
                     s_drain(&S.full[gg % kSStages], (gg / kSStages) & 1, err);
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer (lane 0) + tail zeroing (whole warp) ----------------
-        int g = 0, it = 0;
-        bool ok = true;
-        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-            const int e = item / nrb;
-            const int cnt = pl.expert_cnt[e];
-            if (cnt == 0) continue;
-            const int nk = (cnt + kSK - 1) / kSK;
-            for (int cb = 0; cb < ncb && ok; ++cb, ++it) {
-                const int c0 = cb * kSN;
-                const int nb = min(4, (C - c0) / 64);
-                const uint32_t idesc = idesc_mn(kSM, nb * 64);
-                const int buf = it & 1;
-                ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err);
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                tc_fence_after();
-                for (int kb = 0; kb < nk; ++kb, ++g) {
-                    const int st = g % kSStages;
-                    ok = mbar_wait(&S.full[st], (g / kSStages) & 1, abort_flag, err);
-                    ok = __all_sync(0xffffffffu, ok);
-                    if (!ok) break;
-                    unsigned char *stage = sb + (size_t)st * kStage;
-                    const int rem = min(kSK, cnt - kb * kSK);
-                    if (rem < kSK) {
-                        // slots [rem, 64) of this block belong to the next expert (or lie
-                        // past the routed slots): zero them in every box of the stage
-                        const int nbox = 2 + nb;
-                        const int per_box = (kSK - rem) * 8;          // 16-byte chunks
-                        for (int i = lane; i < nbox * per_box; i += 32) {
-                            const int bx = i / per_box, k = i % per_box;
-                            *reinterpret_cast<uint4 *>(stage + bx * kBox + rem * 128 + k * 16) =
-                                make_uint4(0, 0, 0, 0);
-                        }
-                        fence_proxy_async();
-                    }
-                    __syncwarp();
-                    if (lane == 0) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int g = 0, it = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                const int e = item / nrb;
+                const int cnt = pl.expert_cnt[e];
+                if (cnt == 0) continue;
+                const int nk = (cnt + kSK - 1) / kSK;
+                for (int cb = 0; cb < ncb && ok; ++cb, ++it) {
+                    const int c0 = cb * kSN;
+                    const int nb = min(4, (C - c0) / 64);
+                    const uint32_t idesc = idesc_mn(kSM, nb * 64);
+                    const int buf = it & 1;
+                    if (!mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
+                    tc_fence_after();
+                    for (int kb = 0; kb < nk; ++kb, ++g) {
+                        const int st = g % kSStages;
+                        const int rem = min(kSK, cnt - kb * kSK);
+                        // stages reach the MMA through the fixer warp (fixed[st] completes
+                        // once per fill, after any ragged-tail zeroing)
+                        if (!mbar_wait(&S.fixed[st], (g / kSStages) & 1, abort_flag, err)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t a_s = smem_u32(stage), b_s = a_s + kAStage;
+                        const uint32_t a_s = smem_u32(sb + (size_t)st * kStage), b_s = a_s + kAStage;
                         const int nks = (rem + 15) / 16;
                         for (int kk = 0; kk < nks; ++kk)
                             mma_ss(tbase + buf * kSN, desc_mn_sw128(a_s + kk * 2048),
                                    desc_mn_sw128(b_s + kk * 2048), idesc, (kb | kk) != 0);
                         mma_commit(&S.empty[st]);
                     }
-                    __syncwarp();
+                    if (!ok) break;
+                    mma_commit(&S.acc_full[buf]);
                 }
-                if (!ok) break;
-                if (lane == 0) mma_commit(&S.acc_full[buf]);
             }
-        }
-        // every MMA this CTA issued has completed before TMEM is released
-        if (lane == 0) {
+            // every MMA this CTA issued has completed before TMEM is released
             mma_commit(&S.mma_done);
             s_drain(&S.mma_done, 0, err);
         }
         __syncwarp();
-    } else {
+    } else if (warp == 6) {
+        // ---------------- fixer: forwards every filled stage to the MMA ----------------
+        // Slots past the expert's end inside the last 16-slot group of its last
+        // k-block belong to the next expert (or lie past the routed slots).  The
+        // MMA reads whole 16-slot groups, so those rows are zeroed in every box
+        // of the stage first.  Forwarding every fill (not only ragged ones) keeps
+        // this warp in step with the stage phases.
+        int g = 0;
+        bool ok = true;
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+            const int e = item / nrb;
+            const int cnt = pl.expert_cnt[e];
+            if (cnt == 0) continue;
+            const int nk = (cnt + kSK - 1) / kSK;
+            const int rem = cnt - (nk - 1) * kSK;
+            for (int cb = 0; cb < ncb && ok; ++cb) {
+                const int nb = min(4, (C - cb * kSN) / 64);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int st = g % kSStages;
+                    const uint32_t par = (g / kSStages) & 1;
+                    if (kb == nk - 1 && (rem % 16)) {
+                        ok = mbar_wait(&S.full[st], par, abort_flag, err);
+                        ok = __all_sync(0xffffffffu, ok);
+                        if (!ok) break;
+                        const int r1 = (rem + 15) & ~15;
+                        const int per_box = (r1 - rem) * 8;       // 16-byte chunks
+                        unsigned char *stage = sb + (size_t)st * kStage;
+                        for (int i = lane; i < (2 + nb) * per_box; i += 32) {
+                            const int bx = i / per_box, k = i % per_box;
+                            *reinterpret_cast<uint4 *>(stage + bx * kBox + rem * 128 + k * 16) =
+                                make_uint4(0, 0, 0, 0);
+                        }
+                        fence_proxy_async();
+                        __syncwarp();
+                    } else {
+                        int w_ok = 1;
+                        if (lane == 0) w_ok = mbar_wait(&S.full[st], par, abort_flag, err);
+                        ok = __shfl_sync(0xffffffffu, w_ok, 0) != 0;
+                        if (!ok) break;
+                    }
+                    if (lane == 0) mbar_arrive(&S.fixed[st]);
+                }
+            }
+        }
+    } else if (warp >= 2) {
         // ---------------- epilogue (warps 2-5) ----------------
         const int q = warp & 3;                      // TMEM lane quarter
         const int rr = q * 32 + lane;                // row inside the tile
@@ -265,33 +293,40 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 if (!mbar_wait(&S.acc_full[buf], (it >> 1) & 1, abort_flag, err)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    if (j >= nch) break;
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tbase + lane_off + buf * kSN + j * 32, v);
+                for (int h = 0; h < 2; ++h) {
+                    if (4 * h >= nch) break;
+                    uint32_t v[4][32];
+                    // four 32-column loads in flight, one wait (nch is a multiple of 4)
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        tmem_ld_32x32b_x32(tbase + lane_off + buf * kSN + (4 * h + u) * 32, v[u]);
                     tmem_wait_ld();
-                    if (EPI == EPI_SPARSE) {
-                        uint32_t m = mw[j];
-                        if (m) {
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) my_row[i] = __uint_as_float(v[i]);
-                            // chunk j holds columns with (c/32) % 2 == j % 2: CSR half j&1
-                            int p = (j & 1) ? p1 : p0;
-                            while (m) {
-                                const int b = __ffs(m) - 1;
-                                m &= m - 1;
-                                out[p++] = round_bf16(my_row[b]);
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = 4 * h + u;
+                        if (EPI == EPI_SPARSE) {
+                            uint32_t m = mw[j];
+                            if (m) {
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) my_row[i] = __uint_as_float(v[u][i]);
+                                // chunk j holds columns with (c/32) % 2 == j % 2: CSR half j&1
+                                int p = (j & 1) ? p1 : p0;
+                                while (m) {
+                                    const int b = __ffs(m) - 1;
+                                    m &= m - 1;
+                                    out[p++] = round_bf16(my_row[b]);
+                                }
+                                if (j & 1) p1 = p; else p0 = p;
                             }
-                            if (j & 1) p1 = p; else p0 = p;
-                        }
-                    } else {
-                        float4 *o = reinterpret_cast<float4 *>(out + grow * C + c0 + j * 32);
+                        } else {
+                            float4 *o = reinterpret_cast<float4 *>(out + grow * C + c0 + j * 32);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            o[i] = make_float4(fabsf(round_bf16(__uint_as_float(v[4 * i]))),
-                                               fabsf(round_bf16(__uint_as_float(v[4 * i + 1]))),
-                                               fabsf(round_bf16(__uint_as_float(v[4 * i + 2]))),
-                                               fabsf(round_bf16(__uint_as_float(v[4 * i + 3]))));
+                            for (int i = 0; i < 8; ++i)
+                                o[i] = make_float4(fabsf(round_bf16(__uint_as_float(v[u][4 * i]))),
+                                                   fabsf(round_bf16(__uint_as_float(v[u][4 * i + 1]))),
+                                                   fabsf(round_bf16(__uint_as_float(v[u][4 * i + 2]))),
+                                                   fabsf(round_bf16(__uint_as_float(v[u][4 * i + 3]))));
+                        }
                     }
                 }
                 tc_fence_before();
@@ -375,6 +410,7 @@ int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16
 }  // namespace
 
 bool sddmm_tc_supported(int R, int C) {
+    // C % 128: a tile's column chunks come in groups of four (128 columns)
     return R % kSM == 0 && C % 128 == 0 && s_encode() != nullptr;
 }
 
