@@ -54,7 +54,7 @@ typedef struct {
     int32_t *pair_exp;    /* [P_cap]  expert of each token-major pair          */
     int32_t *pair_slot;   /* [P_cap]  slot of each token-major pair            */
     int32_t *n_pairs;     /* [1]                                               */
-    int32_t *chunk_cnt;   /* [ceil(T/256)*E] scratch                           */
+    int32_t *chunk_cnt;   /* [ceil(T/32)*E] scratch                            */
     int32_t *err;         /* [1]      device error word                        */
 } usaf_route_plan;
 
@@ -156,7 +156,9 @@ int usaf_dispatch(const usaf_route_plan *plan, const void *weights, const void *
 /* usaf_combine replaces the weighted combine (usaf/qwen3moe_dml.py:62,
  * benchmarks/kaggle_t4_bench.py:280-281): y[t] = sum over t's pairs in
  * ascending expert order of fp32(y_seg[slot]) * w, fp32 accumulation, cast
- * to the activation dtype. */
+ * to the activation dtype.  usaf_combine, usaf_combine_bwd and usaf_gather_dx
+ * move rows as 16-byte vectors: H * sizeof(dtype) % 16 == 0 and 16-byte
+ * aligned row buffers, else USAF_EUNSUPPORTED; E <= 1024. */
 int usaf_combine(const usaf_route_plan *plan, const void *y_seg, int32_t dtype, int32_t H,
                  void *y, void *stream);
 

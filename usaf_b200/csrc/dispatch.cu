@@ -3,38 +3,52 @@
 // Dispatch restates benchmarks/kaggle_t4_bench.py:293-306 deterministically:
 // pairs = nonzero(weights) in token-major order, bincount per expert,
 // exclusive cumsum, stable (ascending-token) slot assignment.  Three passes:
-// per-256-token-chunk histograms (shared-memory atomics), one scan block,
-// then a rank pass (warp ballots) that writes both index maps.  The combine
+// per-chunk expert histograms (one warp walks 32 consecutive tokens, each
+// lane owning E/32 experts' counters in registers), one scan block, then a
+// rank pass over the same chunks that writes both index maps.  The combine
 // sums each token's expert outputs in ascending expert order in fp32
 // (usaf/qwen3moe_dml.py:62), so it is deterministic and needs no atomics.
 #include "common.cuh"
 
 namespace usaf {
 
-constexpr int kChunk = 256;
+constexpr int kChunk = 32;   // tokens per dispatch chunk (one warp)
 
-template <typename Act>
-__global__ void __launch_bounds__(kChunk) count_kernel(const Act *__restrict__ w, int T, int E,
-                                                       int32_t *__restrict__ tok_cnt,
-                                                       int32_t *__restrict__ chunk_cnt) {
-    extern __shared__ int32_t hist[];
-    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
-    __syncthreads();
-    int t = blockIdx.x * kChunk + threadIdx.x;
-    if (t < T) {
-        int c = 0;
+// per chunk: tok_cnt[t] = #nonzero weights of token t, chunk_cnt[c][e] = #tokens
+// of the chunk routed to expert e.  Lane l owns experts [l*EPL, l*EPL+EPL).
+template <typename Act, int EPL>
+__global__ void __launch_bounds__(256) count_kernel(const Act *__restrict__ w, int T, int E,
+                                                    int32_t *__restrict__ tok_cnt,
+                                                    int32_t *__restrict__ chunk_cnt) {
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (c * kChunk >= T) return;
+    int cnt[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) cnt[i] = 0;
+    int my_tok = 0;   // lane tt keeps token tt's count
+#pragma unroll 4
+    for (int tt = 0; tt < kChunk; ++tt) {
+        const int t = c * kChunk + tt;
+        if (t >= T) break;
         const Act *row = w + (int64_t)t * E;
-        for (int e = 0; e < E; ++e) {
-            if (to_f(row[e]) != 0.0f) {
-                ++c;
-                atomicAdd(&hist[e], 1);
-            }
+        int mine = 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const int e = lane * EPL + i;
+            const int f = (e < E && to_f(row[e]) != 0.0f) ? 1 : 0;
+            cnt[i] += f;
+            mine += f;
         }
-        tok_cnt[t] = c;
+        const int tot = __reduce_add_sync(0xffffffffu, mine);
+        if (lane == tt) my_tok = tot;
     }
-    __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x)
-        chunk_cnt[(int64_t)blockIdx.x * E + e] = hist[e];
+    if (c * kChunk + lane < T) tok_cnt[c * kChunk + lane] = my_tok;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int e = lane * EPL + i;
+        if (e < E) chunk_cnt[(int64_t)c * E + e] = cnt[i];
+    }
 }
 
 // block-wide exclusive scan of one int per thread (blockDim = 1024)
@@ -106,35 +120,55 @@ __global__ void __launch_bounds__(1024) scan_kernel(usaf_route_plan pl, int nchu
     if (threadIdx.x == 0) pl.tok_off[T] = overflow ? 0 : carry;
 }
 
-template <typename Act>
-__global__ void __launch_bounds__(kChunk) scatter_kernel(usaf_route_plan pl,
-                                                         const Act *__restrict__ w) {
-    __shared__ int warp_cnt[kChunk / 32];
-    int T = pl.T, E = pl.E;
-    int t = blockIdx.x * kChunk + threadIdx.x;
-    int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    const int32_t *base = pl.chunk_cnt + (int64_t)blockIdx.x * E;
-    int p = t < T ? pl.tok_off[t] : 0;
-    for (int e = 0; e < E; ++e) {
-        float wv = t < T ? to_f(w[(int64_t)t * E + e]) : 0.0f;
-        bool f = wv != 0.0f;
-        unsigned bal = __ballot_sync(0xffffffffu, f);
-        if (lane == 0) warp_cnt[wid] = __popc(bal);
-        __syncthreads();
-        int before = 0;
-        for (int i = 0; i < wid; ++i) before += warp_cnt[i];
-        __syncthreads();
-        if (f) {
-            int rank = before + __popc(bal & ((1u << lane) - 1));
-            int slot = base[e] + rank;
-            if (slot < pl.P_cap && p < pl.P_cap) {
-                pl.seg_tok[slot] = t;
-                pl.seg_pair[slot] = p;
-                pl.seg_w[slot] = wv;
-                pl.pair_exp[p] = e;
-                pl.pair_slot[p] = slot;
+// rank pass: the chunk's warp walks its tokens in order; each lane advances
+// the slot counters of its experts (chunk base after the scan), and a token's
+// pairs are numbered in ascending expert order from tok_off[t].
+template <typename Act, int EPL>
+__global__ void __launch_bounds__(256) scatter_kernel(usaf_route_plan pl, const Act *__restrict__ w) {
+    const int T = pl.T, E = pl.E;
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (c * kChunk >= T) return;
+    int run[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+        const int e = lane * EPL + i;
+        run[i] = e < E ? pl.chunk_cnt[(int64_t)c * E + e] : 0;
+    }
+#pragma unroll 2
+    for (int tt = 0; tt < kChunk; ++tt) {
+        const int t = c * kChunk + tt;
+        if (t >= T) break;
+        const Act *row = w + (int64_t)t * E;
+        float wv[EPL];
+        int mine = 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            const int e = lane * EPL + i;
+            wv[i] = e < E ? to_f(row[e]) : 0.0f;
+            mine += wv[i] != 0.0f;
+        }
+        int incl = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int p = pl.tok_off[t] + incl - mine;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+            if (wv[i] != 0.0f) {
+                const int e = lane * EPL + i;
+                const int slot = run[i]++;
+                if (slot < pl.P_cap && p < pl.P_cap) {
+                    pl.seg_tok[slot] = t;
+                    pl.seg_pair[slot] = p;
+                    pl.seg_w[slot] = wv[i];
+                    pl.pair_exp[p] = e;
+                    pl.pair_slot[p] = slot;
+                }
+                ++p;
             }
-            ++p;
         }
     }
 }
@@ -167,62 +201,124 @@ __global__ void gather_rows_scalar(const int32_t *__restrict__ n_pairs,
     }
 }
 
+// 16-byte vector of activations <-> fp32 lanes
+template <typename Act> struct Vec16 {
+    static constexpr int N = 16 / sizeof(Act);
+};
+template <typename Act>
+__device__ __forceinline__ void unpack16(const uint4 &u, float (&f)[16 / sizeof(Act)]) {
+    const Act *a = reinterpret_cast<const Act *>(&u);
+#pragma unroll
+    for (int i = 0; i < Vec16<Act>::N; ++i) f[i] = to_f(a[i]);
+}
+template <typename Act>
+__device__ __forceinline__ uint4 pack16(const float (&f)[16 / sizeof(Act)]) {
+    uint4 u;
+    Act *a = reinterpret_cast<Act *>(&u);
+#pragma unroll
+    for (int i = 0; i < Vec16<Act>::N; ++i) a[i] = from_f<Act>(f[i]);
+    return u;
+}
+
+constexpr int kMaxTokPairs = 1024;   // pairs of one token staged in shared memory (<= E)
+
 // y[t] = act( sum_{pairs of t, ascending expert} fp32(y_seg[slot]) * w )
+// one block per token; each thread owns 16-byte column vectors
 template <typename Act>
 __global__ void __launch_bounds__(256) combine_kernel(usaf_route_plan pl,
                                                       const Act *__restrict__ yseg, int H,
                                                       Act *__restrict__ y) {
-    int t = blockIdx.x;
-    int b = pl.tok_off[t], e = pl.tok_off[t + 1];
-    for (int h = threadIdx.x; h < H; h += blockDim.x) {
-        float acc = 0.0f;
-        for (int q = b; q < e; ++q) {
-            int s = pl.pair_slot[q];
-            acc = __fadd_rn(acc, __fmul_rn(to_f(yseg[(int64_t)s * H + h]), pl.seg_w[s]));
+    constexpr int V = Vec16<Act>::N;
+    __shared__ int s_slot[kMaxTokPairs];
+    __shared__ float s_w[kMaxTokPairs];
+    const int t = blockIdx.x;
+    const int b = pl.tok_off[t], n = min(pl.tok_off[t + 1] - b, kMaxTokPairs);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int sl = pl.pair_slot[b + i];
+        s_slot[i] = sl;
+        s_w[i] = pl.seg_w[sl];
+    }
+    __syncthreads();
+    const int nv = H / V;
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        float acc[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = 0.0f;
+        for (int q = 0; q < n; ++q) {
+            float f[V];
+            unpack16<Act>(__ldg(reinterpret_cast<const uint4 *>(yseg + (int64_t)s_slot[q] * H) + v), f);
+            const float wq = s_w[q];
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(f[i], wq));
         }
-        y[(int64_t)t * H + h] = from_f<Act>(acc);
+        reinterpret_cast<uint4 *>(y + (int64_t)t * H)[v] = pack16<Act>(acc);
     }
 }
 
 // per slot: dcur = act(dy[t] * w); dw_pair = act(sum_h dy[t,h] * y_seg[s,h])
+// one warp per slot, 16-byte vectors
 template <typename Act>
 __global__ void __launch_bounds__(256) combine_bwd_kernel(usaf_route_plan pl,
                                                           const Act *__restrict__ dy,
                                                           const Act *__restrict__ yseg, int H,
                                                           Act *__restrict__ dcur,
                                                           float *__restrict__ dw_pair) {
-    int P = *pl.n_pairs;
-    int lane = threadIdx.x & 31;
+    constexpr int V = Vec16<Act>::N;
+    const int P = *pl.n_pairs;
+    const int lane = threadIdx.x & 31;
+    const int nv = H / V;
     for (int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; s < P;
          s += (gridDim.x * blockDim.x) >> 5) {
-        int t = pl.seg_tok[s];
-        float w = pl.seg_w[s];
+        const int t = pl.seg_tok[s];
+        const float w = pl.seg_w[s];
+        const uint4 *dyr = reinterpret_cast<const uint4 *>(dy + (int64_t)t * H);
+        const uint4 *ysr = reinterpret_cast<const uint4 *>(yseg + (int64_t)s * H);
+        uint4 *dcr = reinterpret_cast<uint4 *>(dcur + (int64_t)s * H);
         float dot = 0.0f;
-        for (int h = lane; h < H; h += 32) {
-            float g = to_f(dy[(int64_t)t * H + h]);
-            dot = fmaf(g, to_f(yseg[(int64_t)s * H + h]), dot);
-            dcur[(int64_t)s * H + h] = from_f<Act>(__fmul_rn(g, w));
+        for (int v = lane; v < nv; v += 32) {
+            float g[V], yv[V], o[V];
+            unpack16<Act>(__ldg(dyr + v), g);
+            unpack16<Act>(__ldg(ysr + v), yv);
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                dot = fmaf(g[i], yv[i], dot);
+                o[i] = __fmul_rn(g[i], w);
+            }
+            dcr[v] = pack16<Act>(o);
         }
         dot = warp_sum(dot);
         if (lane == 0) dw_pair[pl.seg_pair[s]] = round_to<Act>(dot);
     }
 }
 
+// dx[t] = act( sum_{pairs of t, ascending expert} dx_seg[slot] (+ dx_acc[t]) )
 template <typename Act>
 __global__ void __launch_bounds__(256) gather_dx_kernel(usaf_route_plan pl,
                                                         const Act *__restrict__ dxseg,
                                                         const float *__restrict__ dxacc, int H,
                                                         Act *__restrict__ dx) {
-    int t = blockIdx.x;
-    int b = pl.tok_off[t], e = pl.tok_off[t + 1];
-    for (int h = threadIdx.x; h < H; h += blockDim.x) {
-        float acc = 0.0f;
-        for (int q = b; q < e; ++q) {
-            int s = pl.pair_slot[q];
-            acc = __fadd_rn(acc, to_f(dxseg[(int64_t)s * H + h]));
+    constexpr int V = Vec16<Act>::N;
+    __shared__ int s_slot[kMaxTokPairs];
+    const int t = blockIdx.x;
+    const int b = pl.tok_off[t], n = min(pl.tok_off[t + 1] - b, kMaxTokPairs);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s_slot[i] = pl.pair_slot[b + i];
+    __syncthreads();
+    const int nv = H / V;
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+        float acc[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = 0.0f;
+        for (int q = 0; q < n; ++q) {
+            float f[V];
+            unpack16<Act>(__ldg(reinterpret_cast<const uint4 *>(dxseg + (int64_t)s_slot[q] * H) + v), f);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], f[i]);
         }
-        if (dxacc) acc = __fadd_rn(acc, dxacc[(int64_t)t * H + h]);
-        dx[(int64_t)t * H + h] = from_f<Act>(acc);
+        if (dxacc) {
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = __fadd_rn(acc[i], dxacc[(int64_t)t * H + v * V + i]);
+        }
+        reinterpret_cast<uint4 *>(dx + (int64_t)t * H)[v] = pack16<Act>(acc);
     }
 }
 
@@ -231,11 +327,29 @@ static int dispatch_impl(const usaf_route_plan *pl, const Act *w, const Act *x, 
                          cudaStream_t st) {
     int T = pl->T, E = pl->E;
     if (E > 1024) return USAF_EUNSUPPORTED;
-    int nchunks = (T + kChunk - 1) / kChunk;
-    if (nchunks > 0)
-        count_kernel<Act><<<nchunks, kChunk, E * sizeof(int32_t), st>>>(w, T, E, pl->tok_cnt, pl->chunk_cnt);
+    const int nchunks = (T + kChunk - 1) / kChunk;
+    const unsigned grid = cdiv(nchunks, 8);    // 8 warps (chunks) per block
+    if (nchunks > 0) {
+#define USAF_CNT(EPL) count_kernel<Act, EPL><<<grid, 256, 0, st>>>(w, T, E, pl->tok_cnt, pl->chunk_cnt)
+        if (E <= 32) USAF_CNT(1);
+        else if (E <= 64) USAF_CNT(2);
+        else if (E <= 128) USAF_CNT(4);
+        else if (E <= 256) USAF_CNT(8);
+        else if (E <= 512) USAF_CNT(16);
+        else USAF_CNT(32);
+#undef USAF_CNT
+    }
     scan_kernel<<<1, 1024, 0, st>>>(*pl, nchunks);
-    if (nchunks > 0) scatter_kernel<Act><<<nchunks, kChunk, 0, st>>>(*pl, w);
+    if (nchunks > 0) {
+#define USAF_SCT(EPL) scatter_kernel<Act, EPL><<<grid, 256, 0, st>>>(*pl, w)
+        if (E <= 32) USAF_SCT(1);
+        else if (E <= 64) USAF_SCT(2);
+        else if (E <= 128) USAF_SCT(4);
+        else if (E <= 256) USAF_SCT(8);
+        else if (E <= 512) USAF_SCT(16);
+        else USAF_SCT(32);
+#undef USAF_SCT
+    }
     if (x && xp) {
         size_t row_bytes = (size_t)H * sizeof(Act);
         unsigned grid = 148 * 8;
@@ -252,6 +366,12 @@ static int dispatch_impl(const usaf_route_plan *pl, const Act *w, const Act *x, 
 
 using namespace usaf;
 
+// rows of H activations must start on 16-byte boundaries for the vector kernels
+static bool vec_ok(const void *a, const void *b, int H, int dtype) {
+    const int esz = dtype == USAF_F32 ? 4 : 2;
+    return ((uintptr_t)a & 15) == 0 && ((uintptr_t)b & 15) == 0 && ((int64_t)H * esz) % 16 == 0;
+}
+
 extern "C" int usaf_dispatch(const usaf_route_plan *plan, const void *weights, const void *x,
                              int32_t dtype, int32_t H, void *x_perm, void *stream) {
     USAF_REQUIRE(plan && weights && plan->T >= 0 && plan->E >= 1 && plan->P_cap >= 0);
@@ -267,6 +387,7 @@ extern "C" int usaf_combine(const usaf_route_plan *plan, const void *y_seg, int3
                             int32_t H, void *y, void *stream) {
     USAF_REQUIRE(plan && y_seg && y && H >= 1);
     if (plan->T == 0) return USAF_OK;
+    if (!vec_ok(y_seg, y, H, dtype) || plan->E > kMaxTokPairs) return USAF_EUNSUPPORTED;
     cudaStream_t st = as_stream(stream);
     switch (dtype) {
         case USAF_F32: combine_kernel<float><<<plan->T, 256, 0, st>>>(*plan, (const float *)y_seg, H, (float *)y); break;
@@ -281,6 +402,7 @@ extern "C" int usaf_combine_bwd(const usaf_route_plan *plan, const void *dy, con
                                 int32_t dtype, int32_t H, void *dcur, float *dw_pair,
                                 void *stream) {
     USAF_REQUIRE(plan && dy && y_seg && dcur && dw_pair && H >= 1);
+    if (!vec_ok(dy, y_seg, H, dtype) || !vec_ok(dcur, dcur, H, dtype)) return USAF_EUNSUPPORTED;
     cudaStream_t st = as_stream(stream);
     unsigned grid = 148 * 8;
     switch (dtype) {
@@ -296,6 +418,7 @@ extern "C" int usaf_gather_dx(const usaf_route_plan *plan, const void *dx_seg, c
                               int32_t dtype, int32_t H, void *dx, void *stream) {
     USAF_REQUIRE(plan && dx_seg && dx && H >= 1);
     if (plan->T == 0) return USAF_OK;
+    if (!vec_ok(dx_seg, dx, H, dtype) || plan->E > kMaxTokPairs) return USAF_EUNSUPPORTED;
     cudaStream_t st = as_stream(stream);
     switch (dtype) {
         case USAF_F32: gather_dx_kernel<float><<<plan->T, 256, 0, st>>>(*plan, (const float *)dx_seg, dx_acc, H, (float *)dx); break;

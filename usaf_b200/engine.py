@@ -225,7 +225,7 @@ class MoEBlock:
         i32 = dict(dtype=torch.int32, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
         act = dict(dtype=dt, device=dev)
-        nch = (T + 255) // 256
+        nch = (T + 31) // 32     # dispatch chunks of 32 tokens
         self.tok_cnt = torch.zeros(max(T, 1), **i32)
         self.tok_off = torch.zeros(T + 1, **i32)
         self.expert_cnt = torch.zeros(E, **i32)
