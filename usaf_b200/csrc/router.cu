@@ -415,10 +415,10 @@ extern "C" int usaf_router_bwd(const usaf_route_plan *plan, const void *x, const
         transpose_bf16<<<dim3(cdiv(H, 32), cdiv(T, 32)), dim3(32, 8), 0, st>>>(xb, T, H, w.xT, (int)Tp);
         transpose_bf16<<<dim3(cdiv(H, 32), cdiv(E, 32)), dim3(32, 8), 0, st>>>(wb, E, H, w.wT, E);
         USAF_CHECK_LAUNCH();
-        // dX_r^T [H][T] = W_r^T [H][E] * dl[T][E]^T   (K = E)
-        rc = dense_tc_partials(w.wT, H, E, E, w.dl_bf, T, E, E, (int)Hp, (int)Tp, E, 1, w.part, plan->err, st);
+        // dX_r [T][H] = dl [T][E] * (W_r^T [H][E])^T   (K = E)
+        rc = dense_tc_partials(w.dl_bf, T, E, E, w.wT, H, E, E, (int)Tp, (int)Hp, E, 1, w.part, plan->err, st);
         if (rc) return rc;
-        finalize_partials<<<cdiv((int64_t)T * H, 256), 256, 0, st>>>(w.part, 1, (int)Hp, (int)Tp, H, T, 1,
+        finalize_partials<<<cdiv((int64_t)T * H, 256), 256, 0, st>>>(w.part, 1, (int)Tp, (int)Hp, T, H, 0,
                                                                      FIN_F32, dx_acc, H);
         // dW_r [E][H] = dl^T [E][T] * X^T [H][T]^T   (K = T, split-K 8)
         rc = dense_tc_partials(w.dlT, E, T, (int)Tp, w.xT, H, T, (int)Tp, (int)Ep, (int)Hp, (int)rup(T, 64), 8,

@@ -301,6 +301,47 @@ class MoEBlock:
              ptr(self.dx), st)
         return self.dx, self.dw_r
 
+    # ------------------------------------------ experts with given weights ---
+    def experts_forward(self, x: torch.Tensor, weights: torch.Tensor, gu: Projection,
+                        dn: Projection):
+        """Expert part only: route by the dense [T, E] weights the caller
+        gives (nonzero = routed), as ``dml_qwen3_experts_forward``
+        (usaf/qwen3moe_dml.py:24-64) receives them."""
+        d = self.d
+        assert x.shape == (d.T, d.H) and x.dtype == self.dt and x.is_contiguous()
+        assert weights.shape == (d.T, d.E) and weights.dtype == self.dt and weights.is_contiguous()
+        st = stream()
+        self.weights.copy_(weights)
+        call("usaf_dispatch", self.plan, ptr(self.weights), ptr(x), self.dtc, d.H,
+             ptr(self.x_perm), st)
+        call("usaf_expert_gate_up_fwd", self.plan, gu.struct(), ptr(self.x_perm), self.dtc,
+             ptr(self.gu), ptr(self.h), st)
+        call("usaf_expert_down_fwd", self.plan, dn.struct(), ptr(self.h), self.dtc,
+             ptr(self.y_seg), st)
+        call("usaf_combine", self.plan, ptr(self.y_seg), self.dtc, d.H, ptr(self.y), st)
+        return self.y
+
+    def experts_backward(self, dy: torch.Tensor, gu: Projection, dn: Projection):
+        """Backward of :meth:`experts_forward`: (dX [T, H], dweights [T, E])."""
+        d = self.d
+        assert dy.shape == (d.T, d.H) and dy.dtype == self.dt and dy.is_contiguous()
+        st = stream()
+        call("usaf_combine_bwd", self.plan, ptr(dy), ptr(self.y_seg), self.dtc, d.H,
+             ptr(self.dcur), ptr(self.dw_pair), st)
+        call("usaf_expert_down_bwd", self.plan, dn.struct(), ptr(self.dcur), ptr(self.gu),
+             self.dtc, ptr(self.dgu), st)
+        call("usaf_expert_gate_up_bwd", self.plan, gu.struct(), ptr(self.dgu), self.dtc,
+             ptr(self.dx_seg), st)
+        call("usaf_gather_dx", self.plan, ptr(self.dx_seg), None, self.dtc, d.H, ptr(self.dx), st)
+        # d weights: pair p of token t and expert pair_exp[p] gets dw_pair[p]
+        P = self.n_pairs_host()
+        tok = torch.repeat_interleave(torch.arange(d.T, device=self.device),
+                                      (self.tok_off[1:] - self.tok_off[:-1]).long(),
+                                      output_size=P)
+        dwts = torch.zeros(d.T, d.E, dtype=torch.float32, device=self.device)
+        dwts[tok, self.pair_exp[:P].long()] = self.dw_pair[:P]
+        return self.dx, dwts.to(self.dt)
+
     # ------------------------------------------------- expert weight grads ---
     def sparse_grads(self, gu: Projection, dn: Projection, compact_gu: torch.Tensor,
                      compact_dn: torch.Tensor, scale: float = 1.0):

@@ -1,0 +1,181 @@
+"""Qwen3-MoE block on the B200 kernels (drop-in for usaf/qwen3moe_dml.py).
+
+``patch_qwen3moe_for_b200()`` replaces ``Qwen3MoeSparseMoeBlock.forward`` and
+``Qwen3MoeExperts.forward`` of transformers' modeling_qwen3_moe, as
+``patch_qwen3moe_for_dml()`` does (usaf/qwen3moe_dml.py:89-94).  The block
+forward keeps the reference's semantics (usaf/qwen3moe_dml.py:67-86): router
+logits in the activation dtype, fp32 softmax, threshold mask
+``probs >= k-th largest`` (ties admit more than top_k experts), optional
+renormalisation, weights in the activation dtype, and the expert combine
+summed in fp32 in ascending expert order.
+
+Expert weights are not read from the module's ``gate_up_proj`` /
+``down_proj`` parameters (the reference fills those per forward from its
+int4 cache, train.py:187-197); they come from an int4 store attached with
+:func:`attach_int4_experts`, resident in HBM with the overlay of trained
+coordinates.
+
+Gradient capture keeps the reference protocol (usaf/qwen3moe_dml.py:10-19,
+30-56): when ``experts._grad_capture = (store, prefix)`` is set, the backward
+adds the expert-weight gradients to ``store`` under
+``f"{prefix}.gate_up_proj"`` / ``f"{prefix}.down_proj"``:
+:class:`usaf_b200.moe_loader.SparseGradStore` receives compact gradients at
+its active coordinates (computed without forming the dense gradient),
+:class:`usaf_b200.moe_loader.TopKImportanceStore` receives the dense
+|gradient| of every routed expert.  Other store types raise ``TypeError``
+(the dense CPU buffers of the reference's dict protocol are not produced).
+The router weight receives its gradient through autograd.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from .engine import BlockDims, MoEBlock, Projection
+from .moe_loader import SparseGradStore, TopKImportanceStore
+
+
+def int4_projection(entry, shape, group_size: int = 128, dtype=torch.bfloat16,
+                    device=None) -> Projection:
+    """One q4 entry of the reference's store (a dict with ``q``, ``s``, ``z``
+    or a ``(q, s, z, ...)`` tuple, train.py:175-177) as a device Projection."""
+    if isinstance(entry, dict):
+        q, s, z = entry["q"], entry["s"], entry["z"]
+    else:
+        q, s, z = entry[0], entry[1], entry[2]
+    dev = torch.device(device) if device is not None else torch.device("cuda")
+    return Projection(q.to(dev), s.to(dev), z.to(dev), shape, group_size, dtype)
+
+
+def attach_int4_experts(experts: torch.nn.Module, gate_up: Projection, down: Projection) -> None:
+    """Give a ``Qwen3MoeExperts`` module its int4 expert weights."""
+    if gate_up.E != down.E or gate_up.C != down.R or gate_up.R != 2 * down.C:
+        raise ValueError("gate_up [E,2I,H] and down [E,H,I] shapes do not match")
+    experts._usaf_int4 = (gate_up, down)
+
+
+def _int4_of(experts) -> Tuple[Projection, Projection]:
+    p = getattr(experts, "_usaf_int4", None)
+    if p is None:
+        raise RuntimeError("no int4 expert weights attached (usaf_b200.qwen3moe.attach_int4_experts)")
+    return p
+
+
+def _block_for(owner, T: int, H: int, E: int, I: int, top_k: int, norm: bool, dtype, device,
+               pair_factor: int = 2) -> MoEBlock:
+    """Workspace of one module for T tokens (kept between the forward and
+    the backward; one per module, so layers do not share it).  It holds
+    T * min(E, pair_factor * top_k) routed pairs."""
+    cache: Dict[tuple, MoEBlock] = owner.__dict__.setdefault("_usaf_blocks", {})
+    key = (T, top_k, pair_factor, norm)
+    blk = cache.get(key)
+    if blk is None:
+        blk = MoEBlock(BlockDims(T, H, E, I, top_k, norm, dtype), device, pair_factor)
+        cache[key] = blk
+    return blk
+
+
+def _capture(experts, blk: MoEBlock, gu: Projection, dn: Projection) -> None:
+    cap = getattr(experts, "_grad_capture", None)
+    if cap is None:
+        return
+    store, prefix = cap
+    if isinstance(store, SparseGradStore):
+        n_gu, n_dn = f"{prefix}.gate_up_proj", f"{prefix}.down_proj"
+        for n, p in ((n_gu, gu), (n_dn, dn)):
+            if n in store.compact and p.n_ov != store.compact[n].numel():
+                raise ValueError(f"{n}: overlay and store hold different active sets")
+        empty = torch.empty(0, device=blk.device)
+        gu_s = gu if n_gu in store.compact else _NoOverlay()
+        dn_s = dn if n_dn in store.compact else _NoOverlay()
+        blk.sparse_grads(gu_s, dn_s, store.compact.get(n_gu, empty), store.compact.get(n_dn, empty))
+    elif isinstance(store, TopKImportanceStore):
+        hit = (blk.expert_cnt > 0).nonzero().reshape(-1)
+        for which in ("gate_up_proj", "down_proj"):
+            store.add_dense_abs(f"{prefix}.{which}", blk.dense_abs_grad(which), hit)
+    else:
+        raise TypeError(f"usaf_b200 captures into SparseGradStore / TopKImportanceStore, not {type(store).__name__}")
+
+
+class _NoOverlay:
+    """Stands in for a projection whose gradient the store does not want."""
+    n_ov = 0
+
+
+class _BlockFn(torch.autograd.Function):
+    """Router + experts of one block; saves the routing plan in the module's
+    workspace for the backward."""
+
+    @staticmethod
+    def forward(ctx, hs, w_r, block):
+        gate, experts = block.gate, block.experts
+        gu, dn = _int4_of(experts)
+        T, H = hs.shape
+        blk = _block_for(block, T, H, w_r.shape[0], dn.C, gate.top_k, bool(gate.norm_topk_prob),
+                         hs.dtype, hs.device)
+        y = blk.forward(hs, w_r, gu, dn).clone()
+        ctx.block, ctx.blk = block, blk
+        ctx.save_for_backward(hs, w_r)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        hs, w_r = ctx.saved_tensors
+        blk, block = ctx.blk, ctx.block
+        gu, dn = _int4_of(block.experts)
+        dx, dw_r = blk.backward(dy.contiguous(), hs, w_r, gu, dn)
+        _capture(block.experts, blk, gu, dn)
+        return dx.clone(), (dw_r.clone() if ctx.needs_input_grad[1] else None), None
+
+
+class _ExpertsFn(torch.autograd.Function):
+    """Experts with caller-given dense weights (the reference's
+    ``experts(hidden_states, weights)`` call)."""
+
+    @staticmethod
+    def forward(ctx, hs, weights, experts):
+        gu, dn = _int4_of(experts)
+        T, H = hs.shape
+        # pairs per token, rounded up: the workspace must hold every nonzero weight
+        kmax = max(1, -(-int((weights != 0).sum().item()) // max(T, 1)))
+        blk = _block_for(experts, T, H, weights.shape[1], dn.C, kmax, False, hs.dtype, hs.device,
+                         pair_factor=1)
+        y = blk.experts_forward(hs, weights.contiguous(), gu, dn).clone()
+        ctx.experts, ctx.blk = experts, blk
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        blk, experts = ctx.blk, ctx.experts
+        gu, dn = _int4_of(experts)
+        dx, dwts = blk.experts_backward(dy.contiguous(), gu, dn)
+        _capture(experts, blk, gu, dn)
+        return dx.clone(), (dwts if ctx.needs_input_grad[1] else None), None
+
+
+def b200_qwen3_moe_block_forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+    """``dml_qwen3_moe_block_forward`` (usaf/qwen3moe_dml.py:67-86) on B200."""
+    batch_size, sequence_length, hidden_dim = hidden_states.shape
+    hs = hidden_states.reshape(-1, hidden_dim).contiguous()
+    y = _BlockFn.apply(hs, self.gate.weight, self)
+    return y.view(batch_size, sequence_length, hidden_dim)
+
+
+def b200_qwen3_experts_forward(self, hidden_states: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    """``dml_qwen3_experts_forward`` (usaf/qwen3moe_dml.py:24-64) on B200:
+    ``weights`` is the dense [T, E] routing matrix (zeros off-route).  Only
+    routed (nonzero) entries are computed, so the gradient of ``weights`` is
+    ``dy[t] . y_e[t]`` at routed entries and 0 elsewhere; the reference's
+    dense-masked loop also fills the off-route entries, which its block
+    discards through the routing mask."""
+    return _ExpertsFn.apply(hidden_states.contiguous(), weights, self)
+
+
+def patch_qwen3moe_for_b200():
+    """Install the B200 forwards (affects all model instances), like
+    ``patch_qwen3moe_for_dml`` (usaf/qwen3moe_dml.py:89-94)."""
+    from transformers.models.qwen3_moe import modeling_qwen3_moe
+    modeling_qwen3_moe.Qwen3MoeExperts.forward = b200_qwen3_experts_forward
+    modeling_qwen3_moe.Qwen3MoeSparseMoeBlock.forward = b200_qwen3_moe_block_forward
+    return modeling_qwen3_moe
