@@ -129,7 +129,11 @@ def run_ours(args, rank, world, local_rank):
     orig_call = _lib.call
 
     def step(xs, dys):
-        return layer.train_step(xs, dys)
+        # NVTX range per step: lets a profiler capture exactly one step's launches
+        torch.cuda.nvtx.range_push("usaf_step")
+        out = layer.train_step(xs, dys)
+        torch.cuda.nvtx.range_pop()
+        return out
 
     for _ in range(args.warmup):
         step(x, dy)

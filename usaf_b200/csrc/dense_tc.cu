@@ -51,7 +51,8 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
 // grid: (N/128, M/128, splits); each CTA: one 128x128 tile over its K range
 __global__ void __launch_bounds__(kD_Threads, 1)
     dense_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                    int M, int N, int K, int k_per_split, float *__restrict__ part, int *err) {
+                    int M, int N, int K, int k_per_split, float *__restrict__ part, int64_t ldp,
+                    int64_t split_stride, int m_valid, int *err) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *sb = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -119,18 +120,18 @@ __global__ void __launch_bounds__(kD_Threads, 1)
         const int row = m0 + q * 32 + lane;
         d_drain(&S.acc, 0, err);
         tc_fence_after();
-        float *dst = part + ((size_t)blockIdx.z * M + row) * N + n0;
+        float *dst = part + (int64_t)blockIdx.z * split_stride + (int64_t)row * ldp + n0;
         for (int c0 = 0; c0 < kD_BN; c0 += 32) {
             uint32_t v[32];
             tmem_ld_32x32b_x32(tbase + ((uint32_t)(q * 32) << 16) + c0, v);
             tmem_wait_ld();
-            if (nk > 0 && row < M) {
+            if (nk > 0 && row < m_valid) {
 #pragma unroll
                 for (int i = 0; i < 32; i += 4)
                     *reinterpret_cast<float4 *>(dst + c0 + i) =
                         make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]),
                                     __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-            } else if (row < M) {
+            } else if (row < m_valid) {
 #pragma unroll
                 for (int i = 0; i < 32; i += 4)
                     *reinterpret_cast<float4 *>(dst + c0 + i) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -191,7 +192,30 @@ int dense_tc_partials(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda,
         attr = true;
     }
     dim3 grid(Np / kD_BN, Mp / kD_BM, splits);
-    dense_tc_kernel<<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, kps, part, err);
+    dense_tc_kernel<<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, kps, part, Np,
+                                                       (int64_t)Mp * Np, Mp, err);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
+}
+
+// out[m][n] (fp32, row stride ldo) = A * B^T for m < m_valid, n < Np, one K
+// split: the product lands in its destination without a partial buffer
+// (ldo >= Np, Np a multiple of 128).
+int dense_tc_direct(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda, const __nv_bfloat16 *B,
+                    int b_rows, int b_cols, int ldb, int Mp, int Np, int Kp, float *out, int64_t ldo,
+                    int m_valid, int *err, cudaStream_t st) {
+    if (Mp % kD_BM || Np % kD_BN || Kp % kD_BK || !err || ldo < Np) return USAF_EUNSUPPORTED;
+    CUtensorMap ta, tb;
+    if (!d_tmap(&ta, A, a_rows, a_cols, lda) || !d_tmap(&tb, B, b_rows, b_cols, ldb)) return USAF_EUNSUPPORTED;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(dense_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kD_Smem) != cudaSuccess)
+            return USAF_ECUDA;
+        attr = true;
+    }
+    dim3 grid(Np / kD_BN, Mp / kD_BM, 1);
+    dense_tc_kernel<<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, Kp, out, ldo, 0, m_valid, err);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }

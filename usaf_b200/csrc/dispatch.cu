@@ -79,33 +79,60 @@ __device__ int block_excl_scan(int v, int *smem_warp, int &total) {
     return base + x - v;
 }
 
+// Expert totals, expert offsets, chunk bases (in place in chunk_cnt) and
+// token offsets.  blockDim / E thread groups split the chunks of every expert
+// so the per-chunk loads run in parallel.
 __global__ void __launch_bounds__(1024) scan_kernel(usaf_route_plan pl, int nchunks) {
     __shared__ int warp_s[32];
-    int T = pl.T, E = pl.E;
-    // per-expert totals and exclusive prefix over chunks (in place -> chunk bases)
-    int tot_e = 0;
-    if ((int)threadIdx.x < E) {
-        int e = threadIdx.x;
-        int run = 0;
-        for (int c = 0; c < nchunks; ++c) {
-            int v = pl.chunk_cnt[(int64_t)c * E + e];
-            pl.chunk_cnt[(int64_t)c * E + e] = run;
-            run += v;
+    __shared__ int part_s[1024];
+    __shared__ int eoff_s[1024];
+    const int T = pl.T, E = pl.E;
+    const int nparts = blockDim.x / E;              // E <= 1024
+    const int e = threadIdx.x % E, part = threadIdx.x / E;
+    const bool active = part < nparts;
+    const int cpp = (nchunks + nparts - 1) / nparts;
+    const int c0 = part * cpp, c1 = min(nchunks, c0 + cpp);
+    int sum = 0;
+    if (active)
+        for (int c = c0; c < c1; ++c) sum += pl.chunk_cnt[(int64_t)c * E + e];
+    part_s[threadIdx.x] = active ? sum : 0;
+    __syncthreads();
+    int before = 0, tot_e = 0;
+    if (active) {
+        for (int q = 0; q < nparts; ++q) {
+            const int v = part_s[q * E + e];
+            if (q < part) before += v;
+            tot_e += v;
         }
-        tot_e = run;
     }
     int total;
-    int off_e = block_excl_scan((int)threadIdx.x < E ? tot_e : 0, warp_s, total);
-    bool overflow = total > pl.P_cap;
+    const int off_e = block_excl_scan((int)threadIdx.x < E ? tot_e : 0, warp_s, total);
+    const bool overflow = total > pl.P_cap;
     if ((int)threadIdx.x < E) {
-        pl.expert_cnt[threadIdx.x] = overflow ? 0 : tot_e;
-        pl.expert_off[threadIdx.x] = overflow ? 0 : off_e;
-        for (int c = 0; c < nchunks; ++c) pl.chunk_cnt[(int64_t)c * E + threadIdx.x] += off_e;
+        eoff_s[e] = off_e;
+        pl.expert_cnt[e] = overflow ? 0 : tot_e;
+        pl.expert_off[e] = overflow ? 0 : off_e;
     }
     if (threadIdx.x == 0) {
         pl.expert_off[E] = overflow ? 0 : total;
         pl.n_pairs[0] = overflow ? 0 : total;
         if (overflow) atomicOr(pl.err, USAF_ERR_PAIR_OVERFLOW);
+    }
+    __syncthreads();
+    if (active) {
+        // chunk base = expert offset + tokens of this expert in earlier chunks
+        int run = eoff_s[e] + before;
+        for (int cb = c0; cb < c1; cb += 16) {
+            int v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = cb + i < c1 ? pl.chunk_cnt[(int64_t)(cb + i) * E + e] : 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (cb + i < c1) {
+                    pl.chunk_cnt[(int64_t)(cb + i) * E + e] = run;
+                    run += v[i];
+                }
+        }
     }
     // token offsets
     int carry = 0;

@@ -272,6 +272,9 @@ int dense_tc_partials(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda,
                       const __nv_bfloat16 *B, int b_rows, int b_cols, int ldb, int Mp, int Np,
                       int Kp, int splits, float *part, int *err, cudaStream_t st);
 bool dense_tc_available();
+int dense_tc_direct(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda, const __nv_bfloat16 *B,
+                    int b_rows, int b_cols, int ldb, int Mp, int Np, int Kp, float *out, int64_t ldo,
+                    int m_valid, int *err, cudaStream_t st);
 
 static inline int64_t rup(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
@@ -415,11 +418,18 @@ extern "C" int usaf_router_bwd(const usaf_route_plan *plan, const void *x, const
         transpose_bf16<<<dim3(cdiv(H, 32), cdiv(T, 32)), dim3(32, 8), 0, st>>>(xb, T, H, w.xT, (int)Tp);
         transpose_bf16<<<dim3(cdiv(H, 32), cdiv(E, 32)), dim3(32, 8), 0, st>>>(wb, E, H, w.wT, E);
         USAF_CHECK_LAUNCH();
-        // dX_r [T][H] = dl [T][E] * (W_r^T [H][E])^T   (K = E)
-        rc = dense_tc_partials(w.dl_bf, T, E, E, w.wT, H, E, E, (int)Tp, (int)Hp, E, 1, w.part, plan->err, st);
-        if (rc) return rc;
-        finalize_partials<<<cdiv((int64_t)T * H, 256), 256, 0, st>>>(w.part, 1, (int)Tp, (int)Hp, T, H, 0,
-                                                                     FIN_F32, dx_acc, H);
+        // dX_r [T][H] = dl [T][E] * (W_r^T [H][E])^T   (K = E), straight into dx_acc
+        // when its rows hold whole 128-column tiles
+        if (H % 128 == 0) {
+            rc = dense_tc_direct(w.dl_bf, T, E, E, w.wT, H, E, E, (int)Tp, (int)Hp, E, dx_acc, H, T,
+                                 plan->err, st);
+            if (rc) return rc;
+        } else {
+            rc = dense_tc_partials(w.dl_bf, T, E, E, w.wT, H, E, E, (int)Tp, (int)Hp, E, 1, w.part, plan->err, st);
+            if (rc) return rc;
+            finalize_partials<<<cdiv((int64_t)T * H, 256), 256, 0, st>>>(w.part, 1, (int)Tp, (int)Hp, T, H, 0,
+                                                                         FIN_F32, dx_acc, H);
+        }
         // dW_r [E][H] = dl^T [E][T] * X^T [H][T]^T   (K = T, split-K 8)
         rc = dense_tc_partials(w.dlT, E, T, (int)Tp, w.xT, H, T, (int)Tp, (int)Ep, (int)Hp, (int)rup(T, 64), 8,
                                w.part, plan->err, st);
