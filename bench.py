@@ -31,6 +31,16 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CFG = dict(T=4096, H=2048, E=128, k=8, I=768, frac=0.005, lr=1e-4)
+# DRAM bytes (read + write) of one gate_up launch on this workload, from ncu
+GATE_UP_DRAM_BYTES = 367.4e6 + 127.5e6
+
+
+def gate_up_bytes(n_pairs: int) -> float:
+    """Algorithmic bytes of one gate_up launch: int4 codes + fp16 scales and
+    zeros of all experts, x_perm read, gu and h written (bf16)."""
+    E, H, I = CFG["E"], CFG["H"], CFG["I"]
+    w = E * 2 * I * H
+    return w / 2 + w / 128 * 4 + n_pairs * H * 2 + n_pairs * 2 * I * 2 + n_pairs * I * 2
 METRIC = "training tokens/s per step (Qwen3-30B-A3B-shape, int4, 0.5% sparse)"
 UNIT = "tokens/s"
 
@@ -49,29 +59,41 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle sampling (every 100 ms, with timestamps);
+    :meth:`summary` keeps the samples taken inside the marked timed window."""
+
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu}.csv")
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu),
-                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.5)   # let the sampler start before the timed window opens
         except Exception:
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *a):
         if self.proc is not None:
+            time.sleep(0.2)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -80,13 +102,24 @@ class ClockSampler:
             self.f.close()
 
     def summary(self):
+        import datetime
         try:
-            rows = [r.split(",") for r in open(self.path).read().strip().splitlines()]
-            sm = [float(r[0]) for r in rows if r and r[0].strip().replace(".", "").isdigit()]
-            mx = float(rows[0][1]) if rows else None
+            rows = []
+            for line in open(self.path).read().strip().splitlines():
+                r = [x.strip() for x in line.split(",")]
+                if len(r) < 7:
+                    continue
+                try:
+                    ts = datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                rows.append((ts, r[1:]))
+            win = [r for ts, r in rows if self.t0 is not None and self.t0 - 0.05 <= ts <= self.t1 + 0.05]
+            sm = [float(r[0]) for r in win if r[0].replace(".", "").isdigit()]
+            mx = float(win[0][1]) if win else (float(rows[0][1][1]) if rows else None)
             names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-            reasons = sorted({names[i] for r in rows for i in range(4)
-                              if len(r) > 2 + i and "Active" in r[2 + i] and "Not" not in r[2 + i]})
+            reasons = sorted({names[i] for r in win for i in range(4)
+                              if r[2 + i] == "Active"})
             return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                     "reasons": reasons, "samples": len(sm)}
         except Exception as e:  # noqa: BLE001
@@ -159,11 +192,14 @@ def run_ours(args, rank, world, local_rank):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        clk.mark_start()
         start.record()
         for _ in range(args.steps):
             step(x, dy)
         end.record()
         torch.cuda.synchronize()
+        clk.mark_end()
     eng.call = orig_call
     blk.check()
     ms = start.elapsed_time(end) / args.steps
@@ -225,7 +261,10 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "tensor", "kernel": "usaf_expert_gate_up_fwd (grouped int4 GEMM + SwiGLU)",
                      "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
                      "frac": achieved / tflops, "peak_source": src, "kernel_ms": kern_ms,
-                     "traffic": None},
+                     "traffic": GATE_UP_DRAM_BYTES,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                       "launch of this kernel on this workload (--set full capture)",
+                     "algorithmic_bytes": gate_up_bytes(n_pairs)},
         "gpu_launches": launches * args.steps,
         "launches_per_step": {"usaf_b200": launches, "torch_and_copies": lib_launches},
         "clocks": clk.summary(),
@@ -311,7 +350,7 @@ def cpu_info():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-tokens", type=int, default=192)
