@@ -9,8 +9,11 @@ I=768, bf16 activations, int4 group-128 experts; synthetic seeded data.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N>1 runs under torchrun: each rank owns its own tokens and a full replica of
-the layer (weak scaling); value = all ranks' tokens / max-over-ranks time.
+N>1 runs under torchrun, expert-parallel: every rank routes its own 4096
+tokens, owns E/N experts (int4 weights, overlay, masters, Adam state), and
+NCCL all-to-alls move the routed rows to the owners and back; the router
+gradient is all-reduced (weak scaling: tokens per rank fixed).  value = all
+ranks' tokens / max-over-ranks step time.
 ``--impl reference`` times the CPU restatement of the reference's own path
 (the dense-masked expert loop, usaf/qwen3moe_dml.py:24-86, with capture and
 SparseAdam) on the host cores, on rank 0 only.
@@ -149,14 +152,46 @@ def build_layer(dev, seed: int):
     return layer, x, dy
 
 
+def build_ep_layer(dev, rank: int, world: int):
+    """Expert-parallel layer: the same model on every rank (seed 1), this
+    rank's El = E/world experts, this rank's own token batch (seed 1+rank);
+    importance-selected 0.5 % chosen globally across the shards."""
+    from usaf_b200.engine import Projection
+    from usaf_b200.expert_parallel import ExpertParallelLayer
+    from usaf_b200.quantization import quantize_4bit
+    T, H, E, k, I = CFG["T"], CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    El, e0 = E // world, rank * (E // world)
+    g = torch.Generator(device=dev).manual_seed(1)
+    w_r = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    projs = {}
+    for n, shape in (("gate_up_proj", (E, 2 * I, H)), ("down_proj", (E, H, I))):
+        w = torch.randn(*shape, device=dev, generator=g) * 0.02
+        q, s, z, _ = quantize_4bit(w[e0:e0 + El].contiguous(), 128)
+        del w
+        projs[n] = Projection(q, s, z, (El,) + shape[1:], 128, torch.bfloat16)
+    gt = torch.Generator(device=dev).manual_seed(1 + rank)
+    x = torch.randn(T, H, device=dev, generator=gt).to(torch.bfloat16)
+    dy = torch.randn(T, H, device=dev, generator=gt).to(torch.bfloat16)
+    layer = ExpertParallelLayer(w_r, projs["gate_up_proj"], projs["down_proj"], k, T)
+    active = layer.importance(x, dy, CFG["frac"])
+    layer.init_selection(active, lr=CFG["lr"])
+    torch.cuda.synchronize()
+    return layer, x, dy
+
+
 def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     import usaf_b200  # noqa: F401
     from usaf_b200 import _lib
-    layer, x, dy = build_layer(dev, 1 + rank)
+    import usaf_b200.expert_parallel as epm
+    if world > 1:
+        layer, x, dy = build_ep_layer(dev, rank, world)
+        blk = layer.moe
+    else:
+        layer, x, dy = build_layer(dev, 1 + rank)
+        blk = layer.block
     T = CFG["T"]
-    blk = layer.block
     # timed kernel: the grouped gate_up dequant GEMM (+SwiGLU) of the forward
     k_ev = []
     orig_call = _lib.call
@@ -189,6 +224,7 @@ def run_ours(args, rank, world, local_rank):
 
     import usaf_b200.engine as eng
     eng.call = timed_call
+    epm.call = timed_call
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
@@ -201,10 +237,12 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         clk.mark_end()
     eng.call = orig_call
+    epm.call = orig_call
     blk.check()
     ms = start.elapsed_time(end) / args.steps
     kern_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
-    n_pairs = blk.n_pairs_host()
+    # slots the timed gate_up kernel processes on this rank (owner rows under EP)
+    n_pairs = blk.n_rows_host() if world > 1 else blk.n_pairs_host()
 
     # end-to-end through the public API with host buffers
     xh = x.cpu().pin_memory()
@@ -237,15 +275,17 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
 
-    if world > 1:
-        t = torch.tensor([ms, e2e_ms, kern_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, e2e_ms, kern_ms = t.tolist()
-
     hbm, tflops, src = peaks()
     H, I = CFG["H"], CFG["I"]
     flops = 2.0 * n_pairs * (2 * I) * H
     achieved = flops / (kern_ms * 1e-3) / 1e12
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms, kern_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms, kern_ms = t.tolist()
+        a = torch.tensor([achieved], device=dev)      # the slowest rank's kernel rate
+        torch.distributed.all_reduce(a, op=torch.distributed.ReduceOp.MIN)
+        achieved = float(a.item())
     launches, lib_launches = count_launches(lambda: step(x, dy))
     out = {
         "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
@@ -254,14 +294,15 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights quantized to int4 g128)",
         "config": {"workload": "C2: one Qwen3-30B-A3B MoE layer, fwd+bwd+sparse grads+SparseAdam",
                    "T": T, "H": H, "E": CFG["E"], "top_k": CFG["k"], "I": I, "active_frac": CFG["frac"],
-                   "routed_pairs": n_pairs, "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "routed_pairs": n_pairs,
+                   "parallelism": f"ep{world} (experts sharded, NCCL all-to-all)" if world > 1 else "single",
                    "l2": "working set (~1.5 GB int4 weights + activations) exceeds the 126 MB L2"},
         "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
                 "h2d_bytes_per_step": x.numel() * 2 + dy.numel() * 2, "d2h_bytes_per_step": 4},
         "roofline": {"bound": "tensor", "kernel": "usaf_expert_gate_up_fwd (grouped int4 GEMM + SwiGLU)",
                      "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
                      "frac": achieved / tflops, "peak_source": src, "kernel_ms": kern_ms,
-                     "traffic": GATE_UP_DRAM_BYTES,
+                     "traffic": GATE_UP_DRAM_BYTES if world == 1 else None,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
                                        "launch of this kernel on this workload (--set full capture)",
                      "algorithmic_bytes": gate_up_bytes(n_pairs)},
@@ -275,8 +316,8 @@ def run_ours(args, rank, world, local_rank):
 def count_launches(step_fn):
     """Kernels launched by one step, counted by the CUDA profiler (CUPTI)
     outside the timed region: (this library's kernels, everything else --
-    torch's fills/copies).  A library kernel is any kernel whose name is not
-    one of torch's (at::) or a memcpy/memset."""
+    torch's fills/copies and NCCL's collectives).  A library kernel is any
+    kernel whose name is not torch's (at::), NCCL's or a memcpy/memset."""
     from torch.profiler import ProfilerActivity, profile
     torch.cuda.synchronize()
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
@@ -287,7 +328,8 @@ def count_launches(step_fn):
         if str(ev.device_type) != "DeviceType.CUDA":
             continue
         n = ev.name
-        if n.startswith("Memcpy") or n.startswith("Memset") or "at::" in n or "cub::" in n:
+        if (n.startswith("Memcpy") or n.startswith("Memset") or "at::" in n or "cub::" in n
+                or "nccl" in n.lower()):
             other += 1
         else:
             ours += 1
@@ -385,7 +427,7 @@ def main():
             "nccl", device_id=torch.device("cuda", local_rank),
             timeout=__import__("datetime").timedelta(seconds=120))
     out = run_ours(args, rank, world, local_rank)
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, sec = run_reference_cpu(args.cpu_sample_tokens, 1)
         out["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                                "sample": f"{args.cpu_sample_tokens} tokens of the C2 layer, dense-masked "

@@ -281,6 +281,24 @@ int usaf_build_rowptr(const int64_t *keys, int64_t n, int64_t n_rows, int32_t *r
                       void *stream);
 const char *usaf_version(void);
 
+/* ---- expert parallelism ------------------------------------------------------
+ * No counterpart in the reference (it runs in a single process).  Plan:
+ * rank r of W owns experts [r*El, (r+1)*El), tokens stay data-parallel and an
+ * all-to-all delivers each rank's routed rows (x_perm is expert-major, so the
+ * rows bound for one rank are contiguous).  counts[s*El + e] = rows received
+ * from source rank s for local expert e; the receive buffer is in block order
+ * (s, e), the grouped GEMMs want (e, s).
+ * usaf_ep_permute: inverse == 0 moves received rows into expert-major order
+ * (out[dst(i)] = in[i]); inverse == 1 moves them back (out[i] = in[dst(i)]).
+ * n_rows must equal sum(counts) (else USAF_ERR_BAD_INDEX in *err, nothing
+ * moved); row_bytes % 16 == 0, 16-byte aligned buffers, W*El <= 4096.
+ * usaf_ep_owner_counts: expert_cnt[e] = sum_s counts[s][e], expert_off its
+ * exclusive prefix [El+1], *n_rows (optional) the total. */
+int usaf_ep_permute(const int32_t *counts, int32_t W, int32_t El, int64_t n_rows, const void *in,
+                    void *out, int64_t row_bytes, int32_t inverse, int32_t *err, void *stream);
+int usaf_ep_owner_counts(const int32_t *counts, int32_t W, int32_t El, int32_t *expert_cnt,
+                         int32_t *expert_off, int32_t *n_rows, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,6 +1,6 @@
 """ctypes binding of the C ABI in include/usaf_b200.h.
 
-The shared library is built in-tree (``python -m usaf_b200.build``).  There is
+The shared library is built in-tree (``python usaf_b200/build.py``).  There is
 no fallback: importing an op without the library, or calling one on tensors
 that are not on a CUDA device, raises.
 """
@@ -54,6 +54,8 @@ _SIGS = {
     "usaf_expert_down_fwd": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, I32, P, P]),
     "usaf_expert_down_bwd": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, P, I32, P, P]),
     "usaf_expert_gate_up_bwd": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, I32, P, P]),
+    "usaf_ep_permute": (I32, [P, I32, I32, I64, P, P, I64, I32, P, P]),
+    "usaf_ep_owner_counts": (I32, [P, I32, I32, P, P, P, P]),
     "usaf_sparse_dw": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, P, I32, P, F32T, P, P, P]),
     "usaf_sparse_dw_noalloc": (I32, [C.POINTER(RoutePlan), C.POINTER(QWeight), P, P, I32, P, F32T, P, P]),
     "usaf_expert_dense_dw": (I32, [C.POINTER(RoutePlan), I32, I32, P, P, I32, P, P]),
@@ -74,7 +76,7 @@ def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f"usaf_b200 native library not found at {LIB_PATH}; build it with "
-            "`python -m usaf_b200.build` (nvcc, sm_100a).  There is no CPU fallback.")
+            "`python usaf_b200/build.py` (nvcc, sm_100a).  There is no CPU fallback.")
     lib = C.CDLL(LIB_PATH)
     for name, (res, args) in _SIGS.items():
         fn = getattr(lib, name)

@@ -102,10 +102,11 @@ class TopKImportanceStore:
         self._idx[full_name][int(ei)] = i
 
     def add_dense_abs(self, full_name: str, absg: torch.Tensor,
-                      experts: Optional[torch.Tensor] = None) -> None:
+                      experts: Optional[torch.Tensor] = None, expert_offset: int = 0) -> None:
         """All experts at once from the fused backward: ``absg`` is |grad| as
         fp32 [E, R, C]; experts without routed tokens are skipped like the
-        reference's sparse dispatch (no hook fires for them)."""
+        reference's sparse dispatch (no hook fires for them).  ``absg[e]``
+        is expert ``e + expert_offset`` of the full tensor (an expert shard)."""
         if full_name not in self._vals:
             return
         E = absg.shape[0]
@@ -113,9 +114,10 @@ class TopKImportanceStore:
         k = min(self._k_of(numel_e), numel_e)
         hit = range(E) if experts is None else experts.tolist()
         for ei in hit:
-            v, i = engine.topk_desc(absg[ei].reshape(-1), k, idx_base=int(ei) * numel_e)
-            self._vals[full_name][int(ei)] = v
-            self._idx[full_name][int(ei)] = i
+            eg = int(ei) + expert_offset
+            v, i = engine.topk_desc(absg[ei].reshape(-1), k, idx_base=eg * numel_e)
+            self._vals[full_name][eg] = v
+            self._idx[full_name][eg] = i
 
     def candidates(self, name):
         return dict(self._vals[name]), dict(self._idx[name])
@@ -128,18 +130,32 @@ class TopKImportanceStore:
         for name, shape in self._shapes.items():
             if not self._vals[name]:
                 continue
-            vals = torch.cat(list(self._vals[name].values()))
-            idxs = torch.cat(list(self._idx[name].values()))
+            vals, idxs = self.candidate_list(name)
             k = min(max(1, int(_numel(shape) * frac)), vals.numel())
-            # candidate order by ascending flat index, so equal scores resolve
-            # to the lowest index
-            sk, perm = engine.sort_u32(idxs, torch.arange(idxs.numel(), device=idxs.device))
-            _, sel = engine.topk_desc(vals[perm], k, idx_map=sk.to(torch.int64), want_vals=False)
-            out[name] = sel
+            out[name] = select_candidates(vals, idxs, k)
         return out
+
+    def candidate_list(self, name, device=None):
+        """All candidates of one tensor (scores, flat indices), expert order."""
+        keys = sorted(self._vals[name])
+        if not keys:
+            dev = device if device is not None else "cuda"
+            return (torch.empty(0, dtype=torch.float32, device=dev),
+                    torch.empty(0, dtype=torch.int64, device=dev))
+        return (torch.cat([self._vals[name][e] for e in keys]),
+                torch.cat([self._idx[name][e] for e in keys]))
 
     def n_captured(self) -> int:
         return sum(len(d) for d in self._vals.values())
+
+
+def select_candidates(vals: torch.Tensor, idxs: torch.Tensor, k: int) -> torch.Tensor:
+    """Flat indices of the top ``k`` candidate scores, descending score; equal
+    scores resolve to the lowest flat index (candidates are ordered by index
+    before the select)."""
+    sk, perm = engine.sort_u32(idxs, torch.arange(idxs.numel(), device=idxs.device))
+    _, sel = engine.topk_desc(vals[perm], k, idx_map=sk.to(torch.int64), want_vals=False)
+    return sel
 
 
 class QuantizedExpertCache:
