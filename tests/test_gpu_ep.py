@@ -104,9 +104,10 @@ def _ep_worker(rank, world, port, q):
         sl = slice(rank * T, (rank + 1) * T)
         ep = ExpertParallelMoE(w_r, loc["gate_up_proj"], loc["down_proj"], k, T)
         y = ep.forward(x_all[sl].contiguous(), w_r).clone()
-        dx, dw_r = ep.backward(dy_all[sl].contiguous(), x_all[sl].contiguous(), w_r)
         ce = {n: torch.zeros(loc[n].n_ov, device=dev) for n in loc}
-        ep.sparse_grads(ce["gate_up_proj"], ce["down_proj"])
+        # expert gradients computed while the dX rows travel back (the training path)
+        dx, dw_r = ep.backward(dy_all[sl].contiguous(), x_all[sl].contiguous(), w_r,
+                               compact_gu=ce["gate_up_proj"], compact_dn=ce["down_proj"])
         torch.cuda.synchronize()
         ep.check()
         assert torch.equal(y, y_ref[sl]), "y"

@@ -98,14 +98,29 @@ class ExpertExchange:
         if xp.n_recv:
             self._permute(xp.recv_counts, buf[: xp.n_recv], out[: xp.n_recv], False, self.err)
 
-    def to_sources(self, rows_own: torch.Tensor, xp: ExchangePlan, out: torch.Tensor) -> None:
+    def to_sources(self, rows_own: torch.Tensor, xp: ExchangePlan, out: torch.Tensor,
+                   async_op: bool = False):
         """Inverse of :meth:`to_owners`: rows_own (expert-major, local experts)
-        go back to the ranks and slots they came from."""
+        go back to the ranks and slots they came from.  With ``async_op`` the
+        all-to-all is left in flight (returns its work handle): kernels
+        launched meanwhile overlap it, ``wait()`` orders the stream after it."""
         buf = self._buf("back", xp.n_recv, rows_own)
         if xp.n_recv:
             self._permute(xp.recv_counts, rows_own[: xp.n_recv], buf[: xp.n_recv], True, self.err)
-        dist.all_to_all_single(out[: xp.n_send], buf[: xp.n_recv], xp.send_splits,
-                               xp.recv_splits, group=self.group)
+        return dist.all_to_all_single(out[: xp.n_send], buf[: xp.n_recv], xp.send_splits,
+                                      xp.recv_splits, group=self.group, async_op=async_op)
+
+    def to_owners_start(self, rows_src: torch.Tensor, xp: ExchangePlan):
+        """First half of :meth:`to_owners`: the all-to-all, left in flight."""
+        buf = self._buf("recv", xp.n_recv, rows_src)
+        work = dist.all_to_all_single(buf[: xp.n_recv], rows_src[: xp.n_send], xp.recv_splits,
+                                      xp.send_splits, group=self.group, async_op=True)
+        return work, buf
+
+    def to_owners_finish(self, work, buf: torch.Tensor, xp: ExchangePlan, out: torch.Tensor) -> None:
+        work.wait()
+        if xp.n_recv:
+            self._permute(xp.recv_counts, buf[: xp.n_recv], out[: xp.n_recv], False, self.err)
 
 
 class ExpertParallelMoE:
@@ -184,21 +199,30 @@ class ExpertParallelMoE:
 
     # ---------------------------------------------------------------- bwd ---
     def backward(self, dy: torch.Tensor, x: torch.Tensor, w_r: torch.Tensor,
-                 reduce_router: bool = True):
+                 reduce_router: bool = True, compact_gu: Optional[torch.Tensor] = None,
+                 compact_dn: Optional[torch.Tensor] = None):
+        """dX and the router gradient.  Given compact gradient vectors, the
+        expert-weight gradients (:meth:`sparse_grads`) are computed while the
+        dX rows travel back, and the router backward runs while the output
+        gradients travel to the owners."""
         s, d, xp = self.src, self.src.d, self.xp
         assert dy.shape == (d.T, d.H) and dy.dtype == self.dt and dy.is_contiguous()
         st = stream()
         call("usaf_combine_bwd", s.plan, ptr(dy), ptr(s.y_seg), self.dtc, d.H, ptr(s.dcur),
              ptr(s.dw_pair), st)
+        work, buf = self.x_.to_owners_start(s.dcur, xp)
         call("usaf_router_bwd", s.plan, ptr(x), ptr(w_r), self.dtc, d.H, int(d.norm_topk_prob),
              ptr(s.probs), ptr(s.wsum), ptr(s.weights), ptr(s.dw_pair), ptr(s.dlogits),
              ptr(s.dw_r), ptr(s.dx_acc), ptr(s.router_ws), st)
-        self.x_.to_owners(s.dcur, xp, self.dcur_own)
+        self.x_.to_owners_finish(work, buf, xp, self.dcur_own)
         call("usaf_expert_down_bwd", self.own, self.dn.struct(), ptr(self.dcur_own), ptr(self.gu_own),
              self.dtc, ptr(self.dgu_own), st)
         call("usaf_expert_gate_up_bwd", self.own, self.gu.struct(), ptr(self.dgu_own), self.dtc,
              ptr(self.dx_own), st)
-        self.x_.to_sources(self.dx_own, xp, s.dx_seg)
+        work = self.x_.to_sources(self.dx_own, xp, s.dx_seg, async_op=True)
+        if compact_gu is not None and compact_dn is not None:
+            self.sparse_grads(compact_gu, compact_dn)
+        work.wait()
         call("usaf_gather_dx", s.plan, ptr(s.dx_seg), ptr(s.dx_acc), self.dtc, d.H, ptr(s.dx), st)
         dw_r = s.dw_r
         if reduce_router and self.W > 1:
@@ -335,9 +359,9 @@ class ExpertParallelLayer:
         m = self.moe
         self.store.zero_()
         y = m.forward(x, self.w_r)
-        dx, dw_r = m.backward(dy, x, self.w_r)
         n_gu, n_dn = list(self.names)
-        m.sparse_grads(self.store.compact[n_gu], self.store.compact[n_dn])
+        dx, dw_r = m.backward(dy, x, self.w_r, compact_gu=self.store.compact[n_gu],
+                              compact_dn=self.store.compact[n_dn])
         self.opt.step(compact_grads=self.store.compact, grad_div=float(loss_scale))
         self.router_param.grad = dw_r
         self.router_opt.step(grad_div=float(loss_scale))
