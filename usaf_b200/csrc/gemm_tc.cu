@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             S.abort_flag = 0;
             for (int st = 0; st < kStages; ++st) {
                 mbar_init(&S.full_b[st], 1);
-                mbar_init(&S.full_a[st], 256);
+                mbar_init(&S.full_a[st], 8);
                 mbar_init(&S.empty[st], 1);
             }
             mbar_init(&S.acc, 1);
@@ -354,7 +354,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t szr[32];
                 if (TRANS) {
                     // this k-block's per-row (scale|zero) words arrive with the stage's TMA
-                    if (!mbar_wait(&S.full_b[st], (g / kStages) & 1, abort_flag, err)) { ok = false; return; }
+                    // (warp-uniform outcome: the warp stores to TMEM together below)
+                    const bool w_ok = mbar_wait(&S.full_b[st], (g / kStages) & 1, abort_flag, err);
+                    if (!__all_sync(0xffffffffu, w_ok)) { ok = false; return; }
                     const uint32_t *ring = sz_ring + st * kBK + hf * 32;
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -384,12 +386,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
                     }
                 }
-                if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) { ok = false; return; }
+                const bool e_ok = mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err);
+                if (!__all_sync(0xffffffffu, e_ok)) { ok = false; return; }
                 tc_fence_after();
                 tmem_st_32x32b_x16(tbase + lane_off + kAcol + st * 32 + hf * 16, r);
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&S.full_a[st]);
+                // one arrival per warp (full_a counts the 8 producer warps)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.full_a[st]);
                 ++g;
             };
             for (int kb = 0; kb < nk && ok; kb += 3) {
