@@ -336,19 +336,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             // is refilled with kb+3 right after it is consumed (no register moves
             // of in-flight loads, which would wait for them)
             uint4 a0 = make_uint4(0, 0, 0, 0), a1 = a0, a2 = a0;
-            uint32_t z0 = 0, z1 = 0, z2 = 0;
+            // scale and zero stay in separate registers until their use three
+            // k-blocks later (combining them at load time would wait for the loads)
+            uint2 z0 = make_uint2(0, 0), z1 = z0, z2 = z0;
 #define USAF_LOAD(kb_, A_, Z_)                                                                   \
     do {                                                                                         \
         A_ = __ldg(qrow + (kb_) * 2);                                                            \
         if (!TRANS) {                                                                            \
             int64_t gg = (gbase + (int64_t)(kb_) * kBK) / gs;                                    \
-            Z_ = (uint32_t)__ldg(s_ptr + gg) | ((uint32_t)__ldg(z_ptr + gg) << 16);              \
+            Z_.x = __ldg(s_ptr + gg);                                                            \
+            Z_.y = __ldg(z_ptr + gg);                                                            \
         }                                                                                        \
     } while (0)
             USAF_LOAD(0, a0, z0);
             if (1 < nk) USAF_LOAD(1, a1, z1);
             if (2 < nk) USAF_LOAD(2, a2, z2);
-            auto kstep = [&](int kb, uint4 &A, uint32_t &Z) {
+            auto kstep = [&](int kb, uint4 &A, uint2 &Z) {
                 const int st = g % kStages;
                 const int kh0 = kb * kBK + hf * 32;   // first K index of this lane's half-block
                 uint32_t szr[32];
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t m2 = qv0 | (qv0 << 16);
                 const uint32_t sel = (rel & 1) ? 0x5410u : 0x3254u;
                 uint32_t r[16];
-                dequant16<TRANS>(A, Z, szr, pj, m2, sel, r);
+                dequant16<TRANS>(A, Z.x | (Z.y << 16), szr, pj, m2, sel, r);
                 if (kb + 3 < nk) USAF_LOAD(kb + 3, A, Z);   // refill the consumed slot
                 if (hit) {
                     // advance the queue; more coordinates in this block take the slow path
