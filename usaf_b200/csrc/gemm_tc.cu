@@ -501,11 +501,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int q = 0; q < 8; ++q) {
                                 float dh = __bfloat162float(d8[q]);
                                 float gf = __bfloat162float(g8[q]), uf = __bfloat162float(u8[q]);
-                                const float den = __fadd_rn(1.0f, expf(-gf));
-                                float sg_ = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(gf, den)));
+                                // fast exp / reciprocal: the backward products are
+                                // rounded to bf16, a few fp32 ulps do not survive that
+                                const float den = 1.0f + __expf(-gf);
+                                const float sig = __fdividef(1.0f, den);
+                                float sg_ = __bfloat162float(__float2bfloat16_rn(gf * sig));
                                 float ds = __bfloat162float(__float2bfloat16_rn(__fmul_rn(dh, uf)));
                                 du8[q] = __float2bfloat16_rn(__fmul_rn(dh, sg_));
-                                float sig = __frcp_rn(den);   // 1/den, correctly rounded like 1.0f/den
                                 float tt = __fadd_rn(1.0f, __fmul_rn(gf, __fsub_rn(1.0f, sig)));
                                 dg8[q] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(ds, sig), tt));
                             }
