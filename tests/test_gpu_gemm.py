@@ -21,7 +21,7 @@ def dev():
     return torch.device("cuda:0")
 
 
-def make_case(dev, T, H, E, k, I, zipf=None, seed=0, ov_frac=0.005):
+def make_case(dev, T, H, E, k, I, zipf=None, seed=0, ov_frac=0.005, skew=False):
     from usaf_b200.engine import BlockDims, MoEBlock, Projection
     from usaf_b200.quantization import quantize_4bit
     g = torch.Generator(device=dev).manual_seed(seed)
@@ -39,6 +39,17 @@ def make_case(dev, T, H, E, k, I, zipf=None, seed=0, ov_frac=0.005):
         p_ = Projection(q, s, z, shape, 128, torch.bfloat16)
         numel = p_.numel()
         idx = torch.randperm(numel, device=dev, generator=g)[: max(1, int(numel * ov_frac))]
+        if skew:
+            # whole storage rows and columns selected: 32 coordinates in one
+            # 32-wide half block, for the forward and for the transposed backward
+            Rr, Cc = shape[1], shape[2]
+            rows = torch.randint(0, E * Rr, (3,), device=dev, generator=g)
+            cols = torch.randint(0, Cc, (3,), device=dev, generator=g)
+            ee = torch.randint(0, E, (3,), device=dev, generator=g)
+            heavy_r = (rows[:, None] * Cc + torch.arange(Cc, device=dev)[None, :]).reshape(-1)
+            heavy_c = ((ee[:, None] * Rr + torch.arange(Rr, device=dev)[None, :]) * Cc + cols[:, None]).reshape(-1)
+            idx = torch.unique(torch.cat([idx, heavy_r, heavy_c]))
+            idx = idx[torch.randperm(idx.numel(), device=dev, generator=g)]
         master = (torch.randn(idx.numel(), device=dev, generator=g) * 0.05)
         p_.set_overlay(idx, master)
         projs[n] = p_
@@ -72,10 +83,11 @@ CASES = [
     dict(T=17, H=512, E=16, k=4, I=256),
     dict(T=2048, H=512, E=16, k=4, I=256, zipf=1.2),   # skewed: experts > 384 tokens
     dict(T=512, H=2048, E=128, k=8, I=768),            # Qwen3-30B-A3B layer shapes
+    dict(T=256, H=512, E=16, k=4, I=256, skew=True),   # fully selected rows and columns
 ]
 
 
-@pytest.mark.parametrize("case", CASES, ids=lambda c: "T{T}_H{H}_E{E}_I{I}".format(**c) + ("_zipf" if "zipf" in c else ""))
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "T{T}_H{H}_E{E}_I{I}".format(**c) + ("_zipf" if "zipf" in c else "") + ("_skew" if c.get("skew") else ""))
 def test_grouped_gemms_vs_torch(dev, case):
     from usaf_b200 import _lib
     blk, x, w_r, p = make_case(dev, **case)

@@ -77,6 +77,13 @@ def kth_largest(vals: torch.Tensor, k: int) -> torch.Tensor:
     return out
 
 
+def _bitmap(words: torch.Tensor, bits: torch.Tensor, n_words: int) -> torch.Tensor:
+    """int32 words with bit ``bits[i]`` of word ``words[i]`` set (pairs distinct)."""
+    m = torch.zeros(n_words, dtype=torch.int64, device=words.device)
+    m.index_add_(0, words, torch.ones_like(bits) << bits)   # distinct bits: add == or
+    return torch.where(m >= 2 ** 31, m - 2 ** 32, m).to(torch.int32)
+
+
 class Projection:
     """One int4 expert projection resident in HBM, storage shape [E, R, C].
 
@@ -157,11 +164,7 @@ class Projection:
         # the tensor-core gradient epilogue reads a tile's selection from it
         self.ov_mask = None
         if Cc % 32 == 0:
-            words = (e * R + r) * (Cc // 32) + (c >> 5)
-            m = torch.zeros(E * R * (Cc // 32), dtype=torch.int64, device=dev)
-            m.index_add_(0, words, torch.ones_like(c) << (c & 31))   # distinct bits: add == or
-            self.ov_mask = torch.where(m >= 2 ** 31, m - 2 ** 32, m).to(torch.int32)
-            del m, words
+            self.ov_mask = _bitmap((e * R + r) * (Cc // 32) + (c >> 5), c & 31, E * R * (Cc // 32))
         self.val = torch.empty(n, dtype=torch.float32, device=dev)
         self.valT = torch.empty(n, dtype=torch.float32, device=dev)
         self.update_overlay_values(master)
