@@ -4,8 +4,9 @@ expert segment in fp32, rounded to bf16).
 
 Tolerance: the kernels accumulate in fp32 in a different order, so results
 agree to bf16 rounding: max |diff| <= 2 bf16 ulps of the reference value
-(plus 1e-3 absolute slack for values near zero), and relative Frobenius
-error <= 4e-3.
+(4 for the SwiGLU-backward gate gradient, which passes through two rounded
+intermediates), plus 1e-3 absolute slack for values near zero, and relative
+Frobenius error <= 4e-3.
 """
 import pytest
 import torch
@@ -38,7 +39,12 @@ def make_case(dev, T, H, E, k, I, zipf=None, seed=0, ov_frac=0.005, skew=False):
         q, s, z, _ = quantize_4bit(w, 128)
         p_ = Projection(q, s, z, shape, 128, torch.bfloat16)
         numel = p_.numel()
-        idx = torch.randperm(numel, device=dev, generator=g)[: max(1, int(numel * ov_frac))]
+        n_ov = max(1, int(numel * ov_frac))
+        if numel > 1 << 28:   # large tensors: random draws + unique (a full permutation is slow)
+            idx = torch.unique(torch.randint(0, numel, (n_ov,), device=dev, generator=g))
+            idx = idx[torch.randperm(idx.numel(), device=dev, generator=g)]
+        else:
+            idx = torch.randperm(numel, device=dev, generator=g)[:n_ov]
         if skew:
             # whole storage rows and columns selected: 32 coordinates in one
             # 32-wide half block, for the forward and for the transposed backward
@@ -68,12 +74,12 @@ def eff_weight(p):
     return w.view(p.shape).to(torch.bfloat16).float()
 
 
-def check(got, ref, what):
+def check(got, ref, what, ulps=2):
     got, ref = got.float(), ref.float()
-    ulp = ref.abs() * 2 ** -7 * 2 + 1e-3
+    ulp = ref.abs() * 2 ** -7 * ulps + 1e-3
     bad = (got - ref).abs() > ulp
     rel = ((got - ref).norm() / ref.norm().clamp_min(1e-30)).item()
-    assert not bad.any(), f"{what}: {int(bad.sum())} elems beyond 2 ulp; rel {rel:.2e}"
+    assert not bad.any(), f"{what}: {int(bad.sum())} elems beyond {ulps} ulp; rel {rel:.2e}"
     assert rel <= 4e-3, f"{what}: rel {rel:.2e}"
 
 
@@ -84,6 +90,12 @@ CASES = [
     dict(T=2048, H=512, E=16, k=4, I=256, zipf=1.2),   # skewed: experts > 384 tokens
     dict(T=512, H=2048, E=128, k=8, I=768),            # Qwen3-30B-A3B layer shapes
     dict(T=256, H=512, E=16, k=4, I=256, skew=True),   # fully selected rows and columns
+    # C4 sweep points at the Qwen3-30B-A3B shapes (T=1, 16, 256 are covered above at
+    # small H; 4096 with Zipf(1.2) routing, 16384 uniform)
+    dict(T=4096, H=2048, E=128, k=8, I=768, zipf=1.2),
+    dict(T=16384, H=2048, E=128, k=8, I=768),
+    # C5: Mixtral-8x22B-shaped experts (E=8, top-2, H=6144, I=16384)
+    dict(T=256, H=6144, E=8, k=2, I=16384),
 ]
 
 
@@ -147,7 +159,9 @@ def test_grouped_gemms_vs_torch(dev, case):
     sig = 1 / (1 + torch.exp(-g))
     dg_ref = (ds * sig * (1 + g * (1 - sig))).to(torch.bfloat16).float()
     check(blk.dgu[:P, I:], du_ref, "down_bwd/du")
-    check(blk.dgu[:P, :I], dg_ref, "down_bwd/dg")
+    # dg goes through two bf16-rounded intermediates (dh, ds) that may each land
+    # one step away from the reference's: 4 ulps
+    check(blk.dgu[:P, :I], dg_ref, "down_bwd/dg", ulps=4)
     dx_ref = torch.empty(P, H, device=dev)
     for e in range(case["E"]):
         if cnt[e]:
