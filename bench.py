@@ -379,6 +379,69 @@ def run_reference_cpu(sample_tokens: int, iters: int):
     return T / med, med
 
 
+def run_c4_sweep(steps: int = 10):
+    """forward and backward of one C2-shaped layer timed
+    separately at T in {1, 16, 256, 4096, 16384}, uniform and Zipf(1.2)
+    routing (biased router logits: constant feature x[:,0]=1 plus log p_e on
+    w_r[:,0]), random 0.5% overlays; CUDA events, one JSON line per point."""
+    from usaf_b200.engine import BlockDims, MoEBlock, Projection
+    from usaf_b200.quantization import quantize_4bit
+    dev = torch.device("cuda", 0)
+    H, E, k, I = CFG["H"], CFG["E"], CFG["k"], CFG["I"]
+    g = torch.Generator(device=dev).manual_seed(1)
+    projs = {}
+    for n, shape in (("gate_up_proj", (E, 2 * I, H)), ("down_proj", (E, H, I))):
+        w = torch.randn(*shape, device=dev, generator=g) * 0.02
+        q, s_, z, _ = quantize_4bit(w, 128)
+        del w
+        p = Projection(q, s_, z, shape, 128, torch.bfloat16)
+        numel = p.numel()
+        idx = torch.randperm(numel, device=dev, generator=g)[: int(numel * CFG["frac"])]
+        p.set_overlay(idx, torch.randn(idx.numel(), device=dev, generator=g) * 0.02)
+        projs[n] = p
+    gu, dn = projs["gate_up_proj"], projs["down_proj"]
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    for routing in ("uniform", "zipf1.2"):
+        for T in (1, 16, 256, 4096, 16384):
+            x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+            dy = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+            w_r = torch.randn(E, H, device=dev, generator=g) * 0.02
+            if routing != "uniform":
+                x[:, 0] = 1.0
+                pe = torch.arange(1, E + 1, device=dev, dtype=torch.float64) ** -1.2
+                w_r[:, 0] += torch.log(pe / pe.sum()).float()
+            w_r = w_r.to(torch.bfloat16)
+            blk = MoEBlock(BlockDims(T, H, E, I, k, True, torch.bfloat16), dev)
+            cg = torch.zeros(gu.n_ov, device=dev)
+            cd = torch.zeros(dn.n_ov, device=dev)
+            for _ in range(3):
+                blk.forward(x, w_r, gu, dn)
+                blk.backward(dy, x, w_r, gu, dn)
+                blk.sparse_grads(gu, dn, cg, cd)
+            torch.cuda.synchronize()
+            a, b, c = ev(), ev(), ev()
+            tf = tb = 0.0
+            for _ in range(steps):
+                a.record()
+                blk.forward(x, w_r, gu, dn)
+                b.record()
+                blk.backward(dy, x, w_r, gu, dn)
+                blk.sparse_grads(gu, dn, cg, cd)
+                c.record()
+                torch.cuda.synchronize()
+                tf += a.elapsed_time(b)
+                tb += b.elapsed_time(c)
+            blk.check()
+            P = blk.n_pairs_host()
+            fwd_flop = 2.0 * P * 3 * I * H
+            print(json.dumps({"config": "C4", "routing": routing, "T": T, "pairs": P,
+                              "fwd_ms": tf / steps, "bwd_ms": tb / steps,
+                              "fwd_tflops": fwd_flop / (tf / steps * 1e-3) / 1e12,
+                              "bwd_tflops": fwd_flop / (tb / steps * 1e-3) / 1e12,
+                              "max_expert_tokens": int(blk.expert_cnt.max().item())}), flush=True)
+            del blk
+
+
 def cpu_info():
     try:
         for line in open("/proc/cpuinfo"):
@@ -397,9 +460,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-tokens", type=int, default=192)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--c4-sweep", action="store_true",
+                    help="time forward and backward separately over the C4 token sweep (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
+    if args.c4_sweep:
+        run_c4_sweep()
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
