@@ -54,7 +54,7 @@ typedef struct {
     int32_t *pair_exp;    /* [P_cap]  expert of each token-major pair          */
     int32_t *pair_slot;   /* [P_cap]  slot of each token-major pair            */
     int32_t *n_pairs;     /* [1]                                               */
-    int32_t *chunk_cnt;   /* [ceil(T/32)*E] scratch                            */
+    int32_t *chunk_cnt;   /* [ceil(T/16)*E] scratch                            */
     int32_t *err;         /* [1]      device error word                        */
 } usaf_route_plan;
 

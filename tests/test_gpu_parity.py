@@ -177,8 +177,9 @@ def device_flow(inp, dev, active, lr=1e-4):
     layer.block.check()
     return {"y": y.cpu().clone(), "dX": dx.cpu().clone(), "dW_r": dw_r.cpu().clone(),
             "weights": layer.block.weights.cpu().clone(),
-            "compact": {n: layer.store.compact[n].cpu().clone() for n in active},
-            "master_after": {n: layer.masters[n].cpu().clone() for n in active},
+            # the layer keeps compact vectors in CSR order: back to the caller's order
+            "compact": {n: layer.reorder_to(n, layer.store.compact[n], active[n]).cpu() for n in active},
+            "master_after": {n: layer.reorder_to(n, layer.masters[n], active[n]).cpu() for n in active},
             "w_r_after": layer.w_r.cpu().clone(), "layer": layer, "x": x, "dy": dy}
 
 

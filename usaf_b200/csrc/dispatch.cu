@@ -3,7 +3,7 @@
 // Dispatch restates benchmarks/kaggle_t4_bench.py:293-306 deterministically:
 // pairs = nonzero(weights) in token-major order, bincount per expert,
 // exclusive cumsum, stable (ascending-token) slot assignment.  Three passes:
-// per-chunk expert histograms (one warp walks 32 consecutive tokens, each
+// per-chunk expert histograms (one warp walks 16 consecutive tokens, each
 // lane owning E/32 experts' counters in registers), one scan block, then a
 // rank pass over the same chunks that writes both index maps.  The combine
 // sums each token's expert outputs in ascending expert order in fp32
@@ -12,7 +12,7 @@
 
 namespace usaf {
 
-constexpr int kChunk = 32;   // tokens per dispatch chunk (one warp)
+constexpr int kChunk = 16;   // tokens per dispatch chunk (one warp)
 
 // per chunk: tok_cnt[t] = #nonzero weights of token t, chunk_cnt[c][e] = #tokens
 // of the chunk routed to expert e.  Lane l owns experts [l*EPL, l*EPL+EPL).
@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(256) count_kernel(const Act *__restrict__ w, i
         const int tot = __reduce_add_sync(0xffffffffu, mine);
         if (lane == tt) my_tok = tot;
     }
-    if (c * kChunk + lane < T) tok_cnt[c * kChunk + lane] = my_tok;
+    if (lane < kChunk && c * kChunk + lane < T) tok_cnt[c * kChunk + lane] = my_tok;
 #pragma unroll
     for (int i = 0; i < EPL; ++i) {
         const int e = lane * EPL + i;

@@ -129,6 +129,20 @@ class Projection:
     def numel(self) -> int:
         return self.E * self.R * self.C
 
+    def csr_order(self, idx: torch.Tensor) -> torch.Tensor:
+        """Permutation that puts flat indices ``idx`` in the overlay's CSR order
+        (row, 32-column half, column).  A caller that keeps its compact vectors
+        in this order makes every compact <-> CSR map the identity, so the
+        gradient scatter and the optimizer's overlay write-back stream."""
+        idx = idx.reshape(-1).to(device=self.device, dtype=torch.int64)
+        E, R, Cc = self.E, self.R, self.C
+        e = idx // (R * Cc)
+        r = (idx // Cc) % R
+        c = idx % Cc
+        key = ((e * R + r) * 2 + ((c >> 5) & 1)) * Cc + c
+        _, perm = sort_u32(key, torch.arange(idx.numel(), device=self.device, dtype=torch.int64))
+        return perm.long()
+
     def set_overlay(self, idx: torch.Tensor, master: torch.Tensor):
         dev = self.device
         idx = idx.reshape(-1).to(device=dev, dtype=torch.int64)
@@ -228,7 +242,7 @@ class MoEBlock:
         i32 = dict(dtype=torch.int32, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
         act = dict(dtype=dt, device=dev)
-        nch = (T + 31) // 32     # dispatch chunks of 32 tokens
+        nch = (T + 15) // 16     # dispatch chunks of 16 tokens
         self.tok_cnt = torch.zeros(max(T, 1), **i32)
         self.tok_off = torch.zeros(T + 1, **i32)
         self.expert_cnt = torch.zeros(E, **i32)

@@ -333,6 +333,9 @@ class ExpertParallelLayer:
     def init_selection(self, active_local: Dict[str, torch.Tensor], lr=1e-4, weight_decay=0.01,
                        router_lr=None):
         self.active = {n: a.reshape(-1).long() for n, a in active_local.items()}
+        for name, p in self.names.items():   # compact vectors in CSR order (identity maps)
+            if name in self.active:
+                self.active[name] = self.active[name][p.csr_order(self.active[name])]
         self.masters = {}
         for name, p in self.names.items():
             deq = p.dequant(torch.float16).reshape(-1)

@@ -56,7 +56,12 @@ class SparseMoELayer:
 
     def init_selection(self, active: Dict[str, torch.Tensor], lr=1e-4, weight_decay=0.01,
                        router_lr=None):
+        # compact vectors (masters, moments, gradients) in CSR order: the kernels'
+        # compact <-> overlay maps become the identity (streaming accesses)
         self.active = {n: a.reshape(-1).long() for n, a in active.items()}
+        for name, p in self.names.items():
+            if name in self.active:
+                self.active[name] = self.active[name][p.csr_order(self.active[name])]
         self.masters = {}
         for name, p in self.names.items():
             deq = p.dequant(torch.float16).reshape(-1)
@@ -111,8 +116,11 @@ class SparseMoELayer:
         return new_active
 
     def init_selection_from(self, active, masters, lr, weight_decay=0.01):
-        self.active = {n: a.long() for n, a in active.items()}
-        self.masters = dict(masters)
+        self.active, self.masters = {}, {}
+        for name, a in active.items():
+            perm = self.names[name].csr_order(a) if name in self.names else None
+            self.active[name] = a.long() if perm is None else a.long()[perm]
+            self.masters[name] = masters[name] if perm is None else masters[name][perm]
         for name, p in self.names.items():
             p.set_overlay(self.active[name], self.masters[name])
         self.store = SparseGradStore(self.active, self.shapes)
@@ -122,6 +130,16 @@ class SparseMoELayer:
         for name, p in self.names.items():
             self.opt.bind_projection(name, p)
         self.params = params
+
+    def reorder_to(self, name: str, vec: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+        """A compact vector of ``name`` (aligned with ``self.active[name]``, kept in
+        CSR order) re-aligned with the caller's index list ``idx`` (same set)."""
+        a = self.active[name]
+        o_a = torch.argsort(a)
+        o_i = torch.argsort(idx.reshape(-1).to(device=a.device, dtype=torch.long))
+        out = torch.empty_like(vec)
+        out[o_i] = vec[o_a]
+        return out
 
     def _gu_name(self):
         return f"{self.prefix}.gate_up_proj"
