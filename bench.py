@@ -244,33 +244,61 @@ def run_ours(args, rank, world, local_rank):
     # slots the timed gate_up kernel processes on this rank (owner rows under EP)
     n_pairs = blk.n_rows_host() if world > 1 else blk.n_pairs_host()
 
-    # end-to-end through the public API with host buffers
+    # end-to-end: a training loop through the public API with host buffers.  Every
+    # step copies its inputs from pinned host memory and reads its scalar result
+    # (sum(y * dy)) back to the host.  The copy of step i+1's inputs runs on a
+    # second stream while step i computes (two device input buffers), and step
+    # i's result is read once step i+1 has been queued.
     xh = x.cpu().pin_memory()
     dyh = dy.cpu().pin_memory()
-    loss = torch.empty(1, device=dev)
-    lossh = torch.empty(1).pin_memory()
-    xd = torch.empty_like(x)
-    dyd = torch.empty_like(dy)
+    xd = [torch.empty_like(x) for _ in range(2)]
+    dyd = [torch.empty_like(dy) for _ in range(2)]
+    loss = [torch.empty(1, device=dev) for _ in range(2)]
+    lossh = [torch.empty(1).pin_memory() for _ in range(2)]
+    copy_stream = torch.cuda.Stream(device=dev)
+    ev_copied = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    results = []
 
-    def e2e_step():
-        xd.copy_(xh, non_blocking=True)
-        dyd.copy_(dyh, non_blocking=True)
-        y, _, _ = layer.train_step(xd, dyd)
-        _lib.call("usaf_dot", _lib.ptr(y), _lib.ptr(dyd), _lib.BF16, y.numel(), _lib.ptr(loss),
+    def issue_copy(i):
+        b = i % 2
+        with torch.cuda.stream(copy_stream):
+            copy_stream.wait_event(ev_used[b])          # step i-2 is done with buffer b
+            xd[b].copy_(xh, non_blocking=True)
+            dyd[b].copy_(dyh, non_blocking=True)
+            ev_copied[b].record(copy_stream)
+
+    def run_step(i):
+        b = i % 2
+        cur = torch.cuda.current_stream()
+        cur.wait_event(ev_copied[b])
+        y, _, _ = layer.train_step(xd[b], dyd[b])
+        _lib.call("usaf_dot", _lib.ptr(y), _lib.ptr(dyd[b]), _lib.BF16, y.numel(), _lib.ptr(loss[b]),
                   _lib.stream())
-        lossh.copy_(loss, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        return float(lossh.item())
+        lossh[b].copy_(loss[b], non_blocking=True)
+        ev_used[b].record(cur)
 
-    for _ in range(2):
-        e2e_step()
+    def e2e_loop(n):
+        issue_copy(0)
+        for i in range(n):
+            issue_copy(i + 1)
+            run_step(i)
+            if i > 0:
+                ev_used[(i - 1) % 2].synchronize()
+                results.append(float(lossh[(i - 1) % 2].item()))
+        ev_used[(n - 1) % 2].synchronize()
+        results.append(float(lossh[(n - 1) % 2].item()))
+        torch.cuda.current_stream().wait_stream(copy_stream)   # the spare prefetch
+
+    e2e_loop(2)
+    torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        e2e_step()
+    copy_stream.wait_event(e0)      # the first input copy starts inside the timed window
+    e2e_loop(args.steps)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
