@@ -273,7 +273,9 @@ int usaf_sort_u32(const uint32_t *keys_in, const int64_t *vals_in, int64_t n, ui
                   int64_t *vals_out, int32_t descending, void *scratch, void *stream);
 
 /* ---- misc ------------------------------------------------------------------ */
-/* usaf_dot: out[0] = sum_i a[i]*b[i] in fp32 (a, b of dtype). */
+/* usaf_dot: out[0] = sum_i a[i]*b[i] in fp32 (a, b of dtype), reproducible
+ * (fixed reduction order).  Its block partials sit in a fixed array inside
+ * the library: do not run two usaf_dot calls on one device concurrently. */
 int usaf_dot(const void *a, const void *b, int32_t dtype, int64_t n, float *out, void *stream);
 /* usaf_build_rowptr: row_ptr[r] = first position of row r in the sorted
  * row keys (n_rows + 1 entries). */
