@@ -470,6 +470,124 @@ def run_c4_sweep(steps: int = 10):
             del blk
 
 
+def run_c5(steps: int = 10, warmup: int = 3):
+    """BASELINE configs[4] on one GPU: a Mixtral-8x22B-shaped layer (H=6144,
+    E=8, top-2, I=16384, T=4096, int4 g128 experts, bf16): one importance
+    dense-gradient pass, selection of 0.5 %, then sparse training steps
+    (SparseMoELayer.train_step), CUDA events; one JSON line."""
+    from usaf_b200.engine import Projection
+    from usaf_b200.layer import SparseMoELayer
+    from usaf_b200.quantization import quantize_4bit
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T, H, E, k, I, frac = 4096, 6144, 8, 2, 16384, 0.005
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    dy = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    w_r = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    projs = {}
+    for n, shape in (("gate_up_proj", (E, 2 * I, H)), ("down_proj", (E, H, I))):
+        w = torch.randn(*shape, device=dev, generator=g) * 0.02
+        q, s_, z, _ = quantize_4bit(w, 128)
+        del w
+        projs[n] = Projection(q, s_, z, shape, 128, torch.bfloat16)
+    layer = SparseMoELayer(w_r, projs["gate_up_proj"], projs["down_proj"], k, T)
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    layer.importance(x, dy, frac)                       # warm-up of the dense pass
+    torch.cuda.synchronize()
+    a, b = ev(), ev()
+    a.record()
+    store = layer.importance(x, dy, frac)
+    active = store.select(frac)
+    b.record()
+    torch.cuda.synchronize()
+    imp_ms = a.elapsed_time(b)
+    layer.init_selection(active, lr=1e-4)
+    for _ in range(warmup):
+        layer.train_step(x, dy)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(steps):
+        layer.train_step(x, dy)
+    b.record()
+    torch.cuda.synchronize()
+    layer.block.check()
+    ms = a.elapsed_time(b) / steps
+    P = layer.block.n_pairs_host()
+    flop = 2.0 * P * 3 * I * H * 2          # forward + dX backward of the grouped GEMMs
+    print(json.dumps({"config": "C5", "workload": "one Mixtral-8x22B-shaped MoE layer (H 6144, E 8, top-2, "
+                      "I 16384), int4 g128, bf16, T 4096", "importance_pass_ms": imp_ms,
+                      "n_active": sum(a_.numel() for a_ in active.values()),
+                      "step_ms": ms, "tokens_per_s": T / (ms * 1e-3), "pairs": P,
+                      "grouped_gemm_tflops_per_step": flop / (ms * 1e-3) / 1e12,
+                      "steps": steps, "warmup": warmup, "data": "synthetic"}), flush=True)
+
+
+def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2):
+    """BASELINE configs[2] (C3) on one GPU at a reduced depth: a random-init
+    Qwen3MoeForCausalLM with the C3 layer shapes (H 2048, 32/4 heads, head dim
+    128, E 128, top-8, I 768, vocab 151936), int4 g128 experts attached through
+    patch_qwen3moe_for_b200, sequence 2048 x micro-batch 4, LM cross-entropy,
+    trained by usaf_b200.trainer.SparseTrainer (importance pass, 0.5 %
+    selection, loss scaling, SparseAdam + SGD-momentum router).  Attention,
+    norms, embeddings and the LM head run in PyTorch; one JSON line with the
+    whole-model tokens/s and the per-layer time."""
+    from transformers.models.qwen3_moe.configuration_qwen3_moe import Qwen3MoeConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeForCausalLM
+    from usaf_b200 import qwen3moe
+    from usaf_b200.engine import Projection
+    from usaf_b200.quantization import quantize_4bit
+    from usaf_b200.trainer import SparseTrainer
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    qwen3moe.patch_qwen3moe_for_b200()
+    H, E, k, I, V, S, MB = 2048, 128, 8, 768, 151936, 2048, 4
+    cfg = Qwen3MoeConfig(vocab_size=V, hidden_size=H, intermediate_size=6144, num_hidden_layers=n_layers,
+                         num_attention_heads=32, num_key_value_heads=4, head_dim=128,
+                         moe_intermediate_size=I, num_experts=E, num_experts_per_tok=k,
+                         norm_topk_prob=True, max_position_embeddings=4096)
+    torch.manual_seed(3)
+    with torch.device(dev):
+        model = Qwen3MoeForCausalLM(cfg).to(torch.bfloat16)
+    for p_ in model.parameters():
+        p_.requires_grad_(False)
+    g = torch.Generator(device=dev).manual_seed(3)
+    for layer in model.model.layers:
+        mlp = layer.mlp
+        mlp.gate.weight.requires_grad_(True)
+        ps = []
+        for shape in ((E, 2 * I, H), (E, H, I)):
+            w = torch.randn(*shape, device=dev, generator=g) * 0.02
+            q, s_, z, _ = quantize_4bit(w, 128)
+            del w
+            ps.append(Projection(q, s_, z, shape, 128, torch.bfloat16))
+        # the module's own expert tensors are not read by the patched forward
+        mlp.experts.gate_up_proj = torch.nn.Parameter(torch.empty(0, device=dev), requires_grad=False)
+        mlp.experts.down_proj = torch.nn.Parameter(torch.empty(0, device=dev), requires_grad=False)
+        qwen3moe.attach_int4_experts(mlp.experts, *ps)
+    gt = torch.Generator(device=dev).manual_seed(4)
+    batches = [torch.randint(0, V, (MB, S), device=dev, generator=gt) for _ in range(2)]
+    lm = lambda m, ids: m(input_ids=ids, labels=ids).loss  # noqa: E731
+    tr = SparseTrainer(model, steps=1000, lr_peak=2e-4, accum=1, frac=0.005, reselect_every=10 ** 9)
+    tr.init_selection(tr.importance(batches[0], lm))
+    for i in range(warmup):
+        tr.train_step([batches[i % 2]], lm)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    logs = [tr.train_step([batches[i % 2]], lm) for i in range(steps)]
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    print(json.dumps({"config": "C3", "workload": f"Qwen3-30B-A3B-shaped causal LM, {n_layers} of 48 layers "
+                      "(C3 layer shapes), seq 2048 x mb 4, LM cross-entropy, int4 experts, 0.5% sparse, "
+                      "SparseTrainer steps", "layers": n_layers, "tokens_per_step": MB * S,
+                      "step_ms": ms, "tokens_per_s": MB * S / (ms * 1e-3),
+                      "ms_per_layer_incl_head": ms / n_layers, "losses": [round(l_["loss"], 4) for l_ in logs],
+                      "all_finite": all(l_["finite"] for l_ in logs), "steps": steps, "warmup": warmup,
+                      "data": "synthetic (uniform token ids)"}), flush=True)
+
+
 def cpu_info():
     try:
         for line in open("/proc/cpuinfo"):
@@ -490,11 +608,21 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--c4-sweep", action="store_true",
                     help="time forward and backward separately over the C4 token sweep (1 GPU)")
+    ap.add_argument("--c5", action="store_true",
+                    help="Mixtral-8x22B-shaped layer: importance pass + sparse steps (1 GPU)")
+    ap.add_argument("--c3", type=int, default=0, metavar="LAYERS",
+                    help="C3-shaped causal LM with this many layers through SparseTrainer (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     if args.c4_sweep:
         run_c4_sweep()
+        return
+    if args.c5:
+        run_c5()
+        return
+    if args.c3:
+        run_c3(args.c3)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -8,7 +8,8 @@ Qwen3-MoE causal LM patched with patch_qwen3moe_for_b200 and int4 experts:
 * a step with a non-finite loss is skipped (no master, moment or router
   change) and halves the loss scale;
 * a checkpoint written by one trainer and loaded by another restores the
-  active sets, masters, optimizer state and loss-scale state.
+  active sets, masters, optimizer state and loss-scale state;
+* ImportanceScorer scores the int4 experts through the capture protocol.
 """
 import pytest
 import torch
@@ -124,3 +125,34 @@ def test_checkpoint_round_trip(model, tmp_path):
     assert s1["step"] == s2["step"]
     for n in s1["m"]:
         assert torch.equal(s1["m"][n], s2["m"][n]) and torch.equal(s1["v"][n], s2["v"][n])
+
+
+def test_importance_scorer_int4_experts(model):
+    """ImportanceScorer (usaf/importance.py) on the patched model: the int4
+    expert tensors are scored under the reference's parameter names, scores
+    add over batches (two batches = the sum of each alone, bit for bit), and
+    the selectors pick from them on the device."""
+    from usaf_b200.importance import ImportanceScorer
+    from usaf_b200.selector import TopKSelector
+    dev = torch.device("cuda:0")
+    bs = [{"input_ids": ids, "labels": ids} for ids in _batches(2, 77)]
+    gates = {n: p for n, p in model.named_parameters() if n.endswith("mlp.gate.weight")}
+    sc = ImportanceScorer(model, dev, torch.bfloat16, skip_patterns=("embed_tokens", "lm_head", "self_attn",
+                                                                      "norm")).compute_scores(bs)
+    one = [ImportanceScorer(model, dev, torch.bfloat16,
+                            skip_patterns=("embed_tokens", "lm_head", "self_attn", "norm")).compute_scores([b])
+           for b in bs]
+    names = [f"model.layers.{i}.mlp.experts.{w}" for i in range(LAYERS) for w in ("gate_up_proj", "down_proj")]
+    for n in names:
+        shape = (E, 2 * I, H) if n.endswith("gate_up_proj") else (E, H, I)
+        assert sc[n].is_cuda and tuple(sc[n].shape) == shape, n
+        assert sc[n].abs().sum() > 0, n
+        assert torch.equal(sc[n], one[0][n] + one[1][n]), n
+    for n in gates:
+        assert torch.allclose(sc[n], one[0][n] + one[1][n], rtol=1e-6, atol=0), n
+    assert all(not p.requires_grad for p in model.parameters())
+    for p in gates.values():     # the other tests train the gates
+        p.requires_grad_(True)
+    k = 1000
+    masks = TopKSelector(k).select({n: sc[n] for n in names})
+    assert sum(int(m.sum()) for m in masks.values()) >= k

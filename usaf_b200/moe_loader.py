@@ -149,6 +149,36 @@ class TopKImportanceStore:
         return sum(len(d) for d in self._vals.values())
 
 
+class DenseAbsGradStore:
+    """Full-size sums of |gradient| of int4 expert tensors, fp32 [E, R, C] on
+    the device: the importance scores of usaf/importance.py:60-97 for experts
+    whose gradients never exist as a parameter ``.grad`` here.  Filled through
+    the ``_grad_capture`` protocol by the fused backward (every expert, zeros
+    for experts without routed tokens)."""
+
+    def __init__(self, shapes: Dict[str, Any]):
+        self._shapes = dict(shapes)
+        self.scores: Dict[str, torch.Tensor] = {}
+
+    def zero_(self) -> None:
+        self.scores.clear()
+
+    def add_dense_abs(self, full_name: str, absg: torch.Tensor,
+                      experts: Optional[torch.Tensor] = None, expert_offset: int = 0) -> None:
+        if full_name not in self._shapes:
+            return
+        if not absg.is_cuda:
+            raise TypeError("usaf_b200 stores take CUDA gradients")
+        acc = self.scores.get(full_name)
+        if acc is None:
+            acc = torch.zeros(tuple(self._shapes[full_name]), dtype=torch.float32, device=absg.device)
+            self.scores[full_name] = acc
+        acc[expert_offset:expert_offset + absg.shape[0]].add_(absg)
+
+    def n_captured(self) -> int:
+        return len(self.scores)
+
+
 def select_candidates(vals: torch.Tensor, idxs: torch.Tensor, k: int) -> torch.Tensor:
     """Flat indices of the top ``k`` candidate scores, descending score; equal
     scores resolve to the lowest flat index (candidates are ordered by index

@@ -22,7 +22,8 @@ adds the expert-weight gradients to ``store`` under
 :class:`usaf_b200.moe_loader.SparseGradStore` receives compact gradients at
 its active coordinates (computed without forming the dense gradient),
 :class:`usaf_b200.moe_loader.TopKImportanceStore` receives the dense
-|gradient| of every routed expert.  Other store types raise ``TypeError``
+|gradient| of every routed expert, :class:`usaf_b200.moe_loader.DenseAbsGradStore`
+sums it full-size (the importance scores).  Other store types raise ``TypeError``
 (the dense CPU buffers of the reference's dict protocol are not produced).
 The router weight receives its gradient through autograd.
 """
@@ -33,7 +34,7 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from .engine import BlockDims, MoEBlock, Projection
-from .moe_loader import SparseGradStore, TopKImportanceStore
+from .moe_loader import DenseAbsGradStore, SparseGradStore, TopKImportanceStore
 
 
 def int4_projection(entry, shape, group_size: int = 128, dtype=torch.bfloat16,
@@ -94,8 +95,12 @@ def _capture(experts, blk: MoEBlock, gu: Projection, dn: Projection) -> None:
         hit = (blk.expert_cnt > 0).nonzero().reshape(-1)
         for which in ("gate_up_proj", "down_proj"):
             store.add_dense_abs(f"{prefix}.{which}", blk.dense_abs_grad(which), hit)
+    elif isinstance(store, DenseAbsGradStore):
+        for which in ("gate_up_proj", "down_proj"):
+            store.add_dense_abs(f"{prefix}.{which}", blk.dense_abs_grad(which))
     else:
-        raise TypeError(f"usaf_b200 captures into SparseGradStore / TopKImportanceStore, not {type(store).__name__}")
+        raise TypeError("usaf_b200 captures into SparseGradStore / TopKImportanceStore / "
+                        f"DenseAbsGradStore, not {type(store).__name__}")
 
 
 class _NoOverlay:
