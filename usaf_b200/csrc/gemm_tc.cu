@@ -325,12 +325,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int32_t *ov_idx = TRANS ? w.rowT : w.col;
             const float *ov_val = TRANS ? w.valT : w.val;
             int cur = 0, cend = 0, qc0 = 0x7fffffff, qc1 = 0x7fffffff;
-            uint32_t qv0 = 0, qv1 = 0;
+            float qv0 = 0.f, qv1 = 0.f;   // raw values: converted where used, so a queue
+                                          // refill never waits for its own load
             if (w.n_ov > 0) {
                 cur = ov_ptr[crow * 2 + hf];      // this lane's (row, half) segment
                 cend = ov_ptr[crow * 2 + hf + 1];
-                if (cur < cend) { qc0 = ov_idx[cur]; qv0 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur])); }
-                if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
+                if (cur < cend) { qc0 = ov_idx[cur]; qv0 = ov_val[cur]; }
+                if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = ov_val[cur + 1]; }
             }
             // 3-slot prefetch ring: slot i holds k-block kb with kb % 3 == i; a slot
             // is refilled with kb+3 right after it is consumed (no register moves
@@ -370,7 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int rel = qc0 - kh0;
                 const bool hit = rel >= 0 && rel < 32;
                 const int pj = hit ? (rel >> 1) : 0xFF;
-                const uint32_t m2 = qv0 | (qv0 << 16);
+                const uint32_t qb0 = __bfloat16_as_ushort(__float2bfloat16_rn(qv0));
+                const uint32_t m2 = qb0 | (qb0 << 16);
                 const uint32_t sel = (rel & 1) ? 0x5410u : 0x3254u;
                 uint32_t r[16];
                 dequant16<TRANS>(A, Z.x | (Z.y << 16), szr, pj, m2, sel, r);
@@ -380,13 +382,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ++cur;
                     qc0 = qc1; qv0 = qv1;
                     qc1 = 0x7fffffff;
-                    if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
+                    if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = ov_val[cur + 1]; }
                     while (qc0 < kh0 + 32) {
-                        patch_elem16(r, qc0 - kh0, qv0);
+                        patch_elem16(r, qc0 - kh0, __bfloat16_as_ushort(__float2bfloat16_rn(qv0)));
                         ++cur;
                         qc0 = qc1; qv0 = qv1;
                         qc1 = 0x7fffffff;
-                        if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = __bfloat16_as_ushort(__float2bfloat16_rn(ov_val[cur + 1])); }
+                        if (cur + 1 < cend) { qc1 = ov_idx[cur + 1]; qv1 = ov_val[cur + 1]; }
                     }
                 }
                 const bool e_ok = mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err);
