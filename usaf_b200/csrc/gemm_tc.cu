@@ -474,9 +474,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __align__(16) __nv_bfloat16 h8[8];
 #pragma unroll
                             for (int q = 0; q < 8; ++q) {
+                                // fast exp / divide: silu(g) is rounded to bf16 before the
+                                // product, a few fp32 ulps do not survive that rounding
                                 float gf = __bfloat162float(g8[q]);
                                 float sf = __bfloat162float(__float2bfloat16_rn(
-                                    __fdiv_rn(gf, __fadd_rn(1.0f, expf(-gf)))));
+                                    __fdividef(gf, 1.0f + __expf(-gf))));
                                 h8[q] = __float2bfloat16_rn(__fmul_rn(sf, __bfloat162float(u8[q])));
                             }
                             *reinterpret_cast<uint4 *>(out0 + slot * R + j0 + sg * 8) = gv;
