@@ -1,8 +1,10 @@
 // Dense bf16 GEMM on tcgen05 for the router (logits, dW_r, dX_r).
 //
 //   P[split][M][N] = sum_{k in split} A[m][k] * B[n][k]      (fp32 partials)
-// A [M, K] and B [N, K] are row-major bf16 (K contiguous, "K-major"), both
-// staged by TMA with the 128-byte swizzle; one thread issues
+// A [M, K] is row-major bf16 (K contiguous, "K-major"); B is either [N, K]
+// (K-major) or [K, N] (N contiguous, "MN-major": the MMA reads it transposed,
+// so a row-major activation needs no transpose copy).  Both are staged by TMA
+// with the 128-byte swizzle; one thread issues
 // tcgen05.mma kind::f16 (A and B from shared memory, M=128, N=128) into a
 // TMEM accumulator; 4 epilogue warps drain it to fp32 partials.  A separate
 // finalize kernel sums the split-K partials in a fixed order (deterministic)
@@ -48,7 +50,15 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
+// MN-major operand with the 128-byte swizzle: two 64-wide N blocks LBO = 8 KB
+// apart (one TMA box each), 8-row K groups SBO = 1 KB apart, version 1
+__device__ __forceinline__ uint64_t d_desc_mn_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(8192 >> 4) << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
 // grid: (N/128, M/128, splits); each CTA: one 128x128 tile over its K range
+template <bool B_MN>
 __global__ void __launch_bounds__(kD_Threads, 1)
     dense_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                     int M, int N, int K, int k_per_split, float *__restrict__ part, int64_t ldp,
@@ -90,7 +100,12 @@ __global__ void __launch_bounds__(kD_Threads, 1)
                 unsigned char *a_dst = sb + (size_t)st * 2 * kD_TileBytes;
                 const int kx = kbeg + kb * kD_BK;
                 tma_load_2d(a_dst, &tma_a, &S.full[st], kx, m0);
-                tma_load_2d(a_dst + kD_TileBytes, &tma_b, &S.full[st], kx, n0);
+                if (B_MN) {   // two boxes of 64 K rows x 64 N columns
+                    tma_load_2d(a_dst + kD_TileBytes, &tma_b, &S.full[st], n0, kx);
+                    tma_load_2d(a_dst + kD_TileBytes + kD_TileBytes / 2, &tma_b, &S.full[st], n0 + 64, kx);
+                } else {
+                    tma_load_2d(a_dst + kD_TileBytes, &tma_b, &S.full[st], kx, n0);
+                }
                 last = kb;
             }
             if (*abort_flag)
@@ -99,7 +114,8 @@ __global__ void __launch_bounds__(kD_Threads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_bf16(kD_BM, kD_BN);
+            // bit 16: B transposed (MN-major)
+            const uint32_t idesc = idesc_bf16(kD_BM, kD_BN) | (B_MN ? (1u << 16) : 0u);
             for (int kb = 0; kb < nk; ++kb) {
                 const int st = kb % kD_Stages;
                 if (!mbar_wait(&S.full[st], (kb / kD_Stages) & 1, abort_flag, err)) break;
@@ -108,7 +124,8 @@ __global__ void __launch_bounds__(kD_Threads, 1)
                 const uint32_t b_s = a_s + kD_TileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kD_BK / 16; ++kk)
-                    mma_ss(tbase, smem_desc_sw128(a_s + kk * 32), smem_desc_sw128(b_s + kk * 32), idesc,
+                    mma_ss(tbase, smem_desc_sw128(a_s + kk * 32),
+                           B_MN ? d_desc_mn_sw128(b_s + kk * 2048) : smem_desc_sw128(b_s + kk * 32), idesc,
                            (kb | kk) != 0);
                 mma_commit(&S.empty[st]);
             }
@@ -159,41 +176,59 @@ PFN_cuTensorMapEncodeTiled_v12000 d_encode() {
 }
 
 // bf16 matrix of `rows` x `cols` valid elements, row stride `ld` elements;
-// boxes of 128 rows x 64 columns; reads past rows/cols are zero-filled by TMA
-bool d_tmap(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld) {
+// boxes of `box_rows` rows x 64 columns; reads past rows/cols are zero-filled by TMA
+bool d_tmap(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows = kD_BM) {
     auto fn = d_encode();
     if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16 || cols > ld) return false;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)kD_BK, (cuuint32_t)kD_BM};
+    cuuint32_t box[2] = {(cuuint32_t)kD_BK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// B operand tensor map: K-major B [b_rows = N, b_cols = K], or MN-major
+// B [b_rows = K, b_cols = N] (boxes of 64 K rows x 64 N columns)
+bool d_tmap_b(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld, bool b_mn) {
+    return b_mn ? d_tmap(m, ptr, rows, cols, ld, 64) : d_tmap(m, ptr, rows, cols, ld);
+}
+
+template <bool B_MN>
+bool d_attr() {
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(dense_tc_kernel<B_MN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kD_Smem) != cudaSuccess)
+            return false;
+        attr = true;
+    }
+    return true;
+}
+
 }  // namespace
 
 // P[split][Mp][Np] partials of A * B^T over K in [0, Kp): A has a_rows x a_cols
-// valid elements (row stride lda), B has b_rows x b_cols (stride ldb); Mp, Np
-// multiples of 128, Kp of 64; everything outside the valid extents reads as 0.
+// valid elements (row stride lda); B has b_rows x b_cols (stride ldb), K-major
+// ([N, K]) or, with b_mn, MN-major ([K, N]); Mp, Np multiples of 128, Kp of 64;
+// everything outside the valid extents reads as 0.
 int dense_tc_partials(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda,
                       const __nv_bfloat16 *B, int b_rows, int b_cols, int ldb, int Mp, int Np,
-                      int Kp, int splits, float *part, int *err, cudaStream_t st) {
+                      int Kp, int splits, float *part, int *err, cudaStream_t st, bool b_mn) {
     if (Mp % kD_BM || Np % kD_BN || Kp % kD_BK || splits < 1 || !err) return USAF_EUNSUPPORTED;
     int kps = ((Kp / kD_BK + splits - 1) / splits) * kD_BK;
     CUtensorMap ta, tb;
-    if (!d_tmap(&ta, A, a_rows, a_cols, lda) || !d_tmap(&tb, B, b_rows, b_cols, ldb)) return USAF_EUNSUPPORTED;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(dense_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kD_Smem) != cudaSuccess)
-            return USAF_ECUDA;
-        attr = true;
-    }
+    if (!d_tmap(&ta, A, a_rows, a_cols, lda) || !d_tmap_b(&tb, B, b_rows, b_cols, ldb, b_mn))
+        return USAF_EUNSUPPORTED;
+    if (!(b_mn ? d_attr<true>() : d_attr<false>())) return USAF_ECUDA;
     dim3 grid(Np / kD_BN, Mp / kD_BM, splits);
-    dense_tc_kernel<<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, kps, part, Np,
-                                                       (int64_t)Mp * Np, Mp, err);
+    if (b_mn)
+        dense_tc_kernel<true><<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, kps, part, Np,
+                                                                 (int64_t)Mp * Np, Mp, err);
+    else
+        dense_tc_kernel<false><<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, kps, part, Np,
+                                                                  (int64_t)Mp * Np, Mp, err);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
@@ -203,19 +238,17 @@ int dense_tc_partials(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda,
 // (ldo >= Np, Np a multiple of 128).
 int dense_tc_direct(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda, const __nv_bfloat16 *B,
                     int b_rows, int b_cols, int ldb, int Mp, int Np, int Kp, float *out, int64_t ldo,
-                    int m_valid, int *err, cudaStream_t st) {
+                    int m_valid, int *err, cudaStream_t st, bool b_mn) {
     if (Mp % kD_BM || Np % kD_BN || Kp % kD_BK || !err || ldo < Np) return USAF_EUNSUPPORTED;
     CUtensorMap ta, tb;
-    if (!d_tmap(&ta, A, a_rows, a_cols, lda) || !d_tmap(&tb, B, b_rows, b_cols, ldb)) return USAF_EUNSUPPORTED;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(dense_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kD_Smem) != cudaSuccess)
-            return USAF_ECUDA;
-        attr = true;
-    }
+    if (!d_tmap(&ta, A, a_rows, a_cols, lda) || !d_tmap_b(&tb, B, b_rows, b_cols, ldb, b_mn))
+        return USAF_EUNSUPPORTED;
+    if (!(b_mn ? d_attr<true>() : d_attr<false>())) return USAF_ECUDA;
     dim3 grid(Np / kD_BN, Mp / kD_BM, 1);
-    dense_tc_kernel<<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, Kp, out, ldo, 0, m_valid, err);
+    if (b_mn)
+        dense_tc_kernel<true><<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, Kp, out, ldo, 0, m_valid, err);
+    else
+        dense_tc_kernel<false><<<grid, kD_Threads, kD_Smem, st>>>(ta, tb, Mp, Np, Kp, Kp, out, ldo, 0, m_valid, err);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }

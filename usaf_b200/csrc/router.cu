@@ -267,32 +267,17 @@ static int launch_router_bwd_token(const usaf_route_plan *pl, const float *dw_pa
 }
 
 
-// ---- tensor-core path (bf16): transposes and split-K finalize -------------
+// ---- tensor-core path (bf16): dense GEMMs and split-K finalize -------------
+// b_mn: B is [K, N] row-major (read transposed by the MMA), else [N, K]
 int dense_tc_partials(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda,
                       const __nv_bfloat16 *B, int b_rows, int b_cols, int ldb, int Mp, int Np,
-                      int Kp, int splits, float *part, int *err, cudaStream_t st);
+                      int Kp, int splits, float *part, int *err, cudaStream_t st, bool b_mn);
 bool dense_tc_available();
 int dense_tc_direct(const __nv_bfloat16 *A, int a_rows, int a_cols, int lda, const __nv_bfloat16 *B,
                     int b_rows, int b_cols, int ldb, int Mp, int Np, int Kp, float *out, int64_t ldo,
-                    int m_valid, int *err, cudaStream_t st);
+                    int m_valid, int *err, cudaStream_t st, bool b_mn);
 
 static inline int64_t rup(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
-
-// dst[c][r] = src[r][c] for a [rows, cols] bf16 matrix (dst row stride ldd)
-__global__ void transpose_bf16(const __nv_bfloat16 *__restrict__ src, int rows, int cols,
-                               __nv_bfloat16 *__restrict__ dst, int ldd) {
-    __shared__ __nv_bfloat16 tile[32][33];
-    int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
-    for (int i = threadIdx.y; i < 32; i += 8) {
-        int r = r0 + i, c = c0 + threadIdx.x;
-        tile[i][threadIdx.x] = (r < rows && c < cols) ? src[(int64_t)r * cols + c] : __float2bfloat16_rn(0.f);
-    }
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += 8) {
-        int c = c0 + i, r = r0 + threadIdx.x;
-        if (c < cols && r < rows) dst[(int64_t)c * ldd + r] = tile[threadIdx.x][i];
-    }
-}
 
 // out[m][n] = round(sum_s part[s][m][n]) in split order; optional transpose
 // (out[n][m]); rounding to bf16 kept as fp32 (logits), bf16 storage (dW_r)
@@ -316,14 +301,14 @@ __global__ void finalize_partials(const float *__restrict__ part, int splits, in
 
 struct RouterWs {
     float *part;
-    __nv_bfloat16 *xT, *wT, *dl_bf, *dlT;
+    __nv_bfloat16 *dl_bf, *dlT;
     int64_t Tp;
 };
 
 static int64_t router_ws_bytes(int T, int H, int E) {
     int64_t Tp = rup(T, 128), Hp = rup(H, 128), Ep = rup(E, 128);
     int64_t part = std::max({(int64_t)4 * Tp * Ep, Hp * Tp, (int64_t)8 * Ep * Hp});
-    return part * 4 + (Hp * Tp + Hp * Ep + Tp * Ep + Ep * Tp) * 2 + 5 * 256;
+    return part * 4 + (Tp * Ep + Ep * Tp) * 2 + 3 * 256;
 }
 
 static RouterWs carve(void *ws, int T, int H, int E) {
@@ -333,8 +318,6 @@ static RouterWs carve(void *ws, int T, int H, int E) {
     auto take = [&](int64_t bytes) { char *r = p; p += (bytes + 255) / 256 * 256; return r; };
     RouterWs w;
     w.part = reinterpret_cast<float *>(take(part * 4));
-    w.xT = reinterpret_cast<__nv_bfloat16 *>(take(Hp * Tp * 2));
-    w.wT = reinterpret_cast<__nv_bfloat16 *>(take(Hp * Ep * 2));
     w.dl_bf = reinterpret_cast<__nv_bfloat16 *>(take(Tp * Ep * 2));
     w.dlT = reinterpret_cast<__nv_bfloat16 *>(take(Ep * Tp * 2));
     w.Tp = Tp;
@@ -380,7 +363,7 @@ extern "C" int usaf_router_fwd(const void *x, const void *w_r, int32_t dtype, in
         RouterWs w = carve(ws, T, H, E);
         int64_t Tp = rup(T, 128), Ep = rup(E, 128);
         int rc = dense_tc_partials((const __nv_bfloat16 *)x, T, H, H, (const __nv_bfloat16 *)w_r, E, H, H,
-                                   (int)Tp, (int)Ep, H, 4, w.part, err, st);
+                                   (int)Tp, (int)Ep, H, 4, w.part, err, st, false);
         if (rc) return rc;
         finalize_partials<<<cdiv((int64_t)T * E, 256), 256, 0, st>>>(w.part, 4, (int)Tp, (int)Ep, T, E, 0,
                                                                      FIN_F32_ROUND_BF16, logits, E);
@@ -414,25 +397,22 @@ extern "C" int usaf_router_bwd(const usaf_route_plan *plan, const void *x, const
         rc = launch_router_bwd_token<__nv_bfloat16>(plan, dw_pair, probs, wsum, (const __nv_bfloat16 *)weights,
                                                     norm, dlogits, w.dl_bf, w.dlT, (int)Tp, st);
         if (rc) return rc;
-        // X^T [H][Tp] and W_r^T [H][E]
-        transpose_bf16<<<dim3(cdiv(H, 32), cdiv(T, 32)), dim3(32, 8), 0, st>>>(xb, T, H, w.xT, (int)Tp);
-        transpose_bf16<<<dim3(cdiv(H, 32), cdiv(E, 32)), dim3(32, 8), 0, st>>>(wb, E, H, w.wT, E);
-        USAF_CHECK_LAUNCH();
-        // dX_r [T][H] = dl [T][E] * (W_r^T [H][E])^T   (K = E), straight into dx_acc
-        // when its rows hold whole 128-column tiles
+        // dX_r [T][H] = dl [T][E] * W_r [E][H]   (K = E, W_r read MN-major), straight
+        // into dx_acc when its rows hold whole 128-column tiles
         if (H % 128 == 0) {
-            rc = dense_tc_direct(w.dl_bf, T, E, E, w.wT, H, E, E, (int)Tp, (int)Hp, E, dx_acc, H, T,
-                                 plan->err, st);
+            rc = dense_tc_direct(w.dl_bf, T, E, E, wb, E, H, H, (int)Tp, (int)Hp, E, dx_acc, H, T,
+                                 plan->err, st, true);
             if (rc) return rc;
         } else {
-            rc = dense_tc_partials(w.dl_bf, T, E, E, w.wT, H, E, E, (int)Tp, (int)Hp, E, 1, w.part, plan->err, st);
+            rc = dense_tc_partials(w.dl_bf, T, E, E, wb, E, H, H, (int)Tp, (int)Hp, E, 1, w.part, plan->err, st,
+                                   true);
             if (rc) return rc;
             finalize_partials<<<cdiv((int64_t)T * H, 256), 256, 0, st>>>(w.part, 1, (int)Tp, (int)Hp, T, H, 0,
                                                                          FIN_F32, dx_acc, H);
         }
-        // dW_r [E][H] = dl^T [E][T] * X^T [H][T]^T   (K = T, split-K 8)
-        rc = dense_tc_partials(w.dlT, E, T, (int)Tp, w.xT, H, T, (int)Tp, (int)Ep, (int)Hp, (int)rup(T, 64), 8,
-                               w.part, plan->err, st);
+        // dW_r [E][H] = dl^T [E][T] * X [T][H]   (K = T, X read MN-major, split-K 8)
+        rc = dense_tc_partials(w.dlT, E, T, (int)Tp, xb, T, H, H, (int)Ep, (int)Hp, (int)rup(T, 64), 8,
+                               w.part, plan->err, st, true);
         if (rc) return rc;
         finalize_partials<<<cdiv((int64_t)E * H, 256), 256, 0, st>>>(w.part, 8, (int)Ep, (int)Hp, E, H, 0,
                                                                      FIN_BF16, dw_r, H);
