@@ -117,6 +117,36 @@ __device__ __forceinline__ void patch_elem16(uint32_t (&r)[16], int c, uint32_t 
     }
 }
 
+// packed fp32 pairs (sm_100 f32x2 arithmetic, round to nearest even)
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ float f2_lo(uint64_t a) { return __uint_as_float((uint32_t)a); }
+__device__ __forceinline__ float f2_hi(uint64_t a) { return __uint_as_float((uint32_t)(a >> 32)); }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// bf16 pair (low half = first element) <-> packed fp32 pair
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) {
+    return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t a) {
+    const __nv_bfloat162 r = __floats2bfloat162_rn(f2_lo(a), f2_hi(a));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -469,22 +499,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const int64_t slot = row0 + c0 + j;
                             uint4 gv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
                             uint4 uv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + 64 + sg * 8);
-                            const __nv_bfloat16 *g8 = reinterpret_cast<const __nv_bfloat16 *>(&gv);
-                            const __nv_bfloat16 *u8 = reinterpret_cast<const __nv_bfloat16 *>(&uv);
-                            __align__(16) __nv_bfloat16 h8[8];
+                            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+                            const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+                            const uint64_t one2 = f2_pack(1.0f, 1.0f);
+                            uint32_t h4[4];
 #pragma unroll
-                            for (int q = 0; q < 8; ++q) {
+                            for (int w2 = 0; w2 < 4; ++w2) {
                                 // fast exp / divide: silu(g) is rounded to bf16 before the
                                 // product, a few fp32 ulps do not survive that rounding
-                                float gf = __bfloat162float(g8[q]);
-                                float sf = __bfloat162float(__float2bfloat16_rn(
-                                    __fdividef(gf, 1.0f + __expf(-gf))));
-                                h8[q] = __float2bfloat16_rn(__fmul_rn(sf, __bfloat162float(u8[q])));
+                                const uint64_t g2 = bf2_to_f2(gw[w2]);
+                                const uint64_t den2 = f2_add(one2, f2_pack(__expf(-f2_lo(g2)), __expf(-f2_hi(g2))));
+                                const uint64_t s2 = f2_pack(__fdividef(f2_lo(g2), f2_lo(den2)),
+                                                            __fdividef(f2_hi(g2), f2_hi(den2)));
+                                h4[w2] = f2_to_bf2(f2_mul(bf2_to_f2(f2_to_bf2(s2)), bf2_to_f2(uw[w2])));
                             }
                             *reinterpret_cast<uint4 *>(out0 + slot * R + j0 + sg * 8) = gv;
                             *reinterpret_cast<uint4 *>(out0 + slot * R + I + j0 + sg * 8) = uv;
-                            *reinterpret_cast<uint4 *>(out1 + slot * I + j0 + sg * 8) =
-                                *reinterpret_cast<const uint4 *>(h8);
+                            *reinterpret_cast<uint4 *>(out1 + slot * I + j0 + sg * 8) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
                         }
                     }
                 } else {  // MODE_DOWN_BWD: SwiGLU backward with the forward's gate/up
@@ -495,28 +526,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
                             const int i0 = h0 + sg * 8;
-                            uint4 dv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
-                            const uint4 gv = gpre[q], uv = upre[q];
-                            const __nv_bfloat16 *d8 = reinterpret_cast<const __nv_bfloat16 *>(&dv);
-                            const __nv_bfloat16 *g8 = reinterpret_cast<const __nv_bfloat16 *>(&gv);
-                            const __nv_bfloat16 *u8 = reinterpret_cast<const __nv_bfloat16 *>(&uv);
-                            __align__(16) __nv_bfloat16 dg8[8], du8[8];
+                            const uint4 dv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
+                            const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+                            const uint32_t gw[4] = {gpre[q].x, gpre[q].y, gpre[q].z, gpre[q].w};
+                            const uint32_t uw[4] = {upre[q].x, upre[q].y, upre[q].z, upre[q].w};
+                            uint32_t dg4[4], du4[4];
+                            const uint64_t one2 = f2_pack(1.0f, 1.0f);
 #pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                float dh = __bfloat162float(d8[q]);
-                                float gf = __bfloat162float(g8[q]), uf = __bfloat162float(u8[q]);
-                                // fast exp / reciprocal: the backward products are
-                                // rounded to bf16, a few fp32 ulps do not survive that
-                                const float den = 1.0f + __expf(-gf);
-                                const float sig = __fdividef(1.0f, den);
-                                float sg_ = __bfloat162float(__float2bfloat16_rn(gf * sig));
-                                float ds = __bfloat162float(__float2bfloat16_rn(__fmul_rn(dh, uf)));
-                                du8[q] = __float2bfloat16_rn(__fmul_rn(dh, sg_));
-                                float tt = __fadd_rn(1.0f, __fmul_rn(gf, __fsub_rn(1.0f, sig)));
-                                dg8[q] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(ds, sig), tt));
+                            for (int w2 = 0; w2 < 4; ++w2) {
+                                // two elements per packed fp32 operation; fast exp / reciprocal:
+                                // the backward products are rounded to bf16, a few fp32 ulps
+                                // do not survive that
+                                const uint64_t dh2 = bf2_to_f2(dw[w2]), g2 = bf2_to_f2(gw[w2]);
+                                const uint64_t u2 = bf2_to_f2(uw[w2]);
+                                const uint64_t den2 = f2_add(one2, f2_pack(__expf(-f2_lo(g2)), __expf(-f2_hi(g2))));
+                                const uint64_t sig2 = f2_pack(__fdividef(1.0f, f2_lo(den2)), __fdividef(1.0f, f2_hi(den2)));
+                                const uint64_t sgr2 = bf2_to_f2(f2_to_bf2(f2_mul(g2, sig2)));
+                                const uint64_t dsr2 = bf2_to_f2(f2_to_bf2(f2_mul(dh2, u2)));
+                                du4[w2] = f2_to_bf2(f2_mul(dh2, sgr2));
+                                const uint64_t tt2 = f2_add(one2, f2_mul(g2, f2_sub(one2, sig2)));
+                                dg4[w2] = f2_to_bf2(f2_mul(f2_mul(dsr2, sig2), tt2));
                             }
-                            *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + i0) = *reinterpret_cast<const uint4 *>(dg8);
-                            *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + I + i0) = *reinterpret_cast<const uint4 *>(du8);
+                            *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + i0) = make_uint4(dg4[0], dg4[1], dg4[2], dg4[3]);
+                            *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + I + i0) = make_uint4(du4[0], du4[1], du4[2], du4[3]);
                         }
                     }
                 }
