@@ -35,7 +35,7 @@ sys.path.insert(0, ROOT)
 
 CFG = dict(T=4096, H=2048, E=128, k=8, I=768, frac=0.005, lr=1e-4)
 # DRAM bytes (read + write) of one gate_up launch on this workload, from ncu
-GATE_UP_DRAM_BYTES = 367.4e6 + 127.5e6
+GATE_UP_DRAM_BYTES = 368.7e6 + 128.5e6
 
 
 def gate_up_bytes(n_pairs: int) -> float:
@@ -259,13 +259,20 @@ def run_ours(args, rank, world, local_rank):
     ev_copied = [torch.cuda.Event() for _ in range(2)]
     ev_used = [torch.cuda.Event() for _ in range(2)]
     results = []
+    copy_ev = []        # (start, end) of each step's input copy, timed loop only
 
     def issue_copy(i):
         b = i % 2
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(ev_used[b])          # step i-2 is done with buffer b
+            if copy_ev is not None:
+                c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                c0.record(copy_stream)
             xd[b].copy_(xh, non_blocking=True)
             dyd[b].copy_(dyh, non_blocking=True)
+            if copy_ev is not None:
+                c1.record(copy_stream)
+                copy_ev.append((c0, c1))
             ev_copied[b].record(copy_stream)
 
     def run_step(i):
@@ -292,6 +299,7 @@ def run_ours(args, rank, world, local_rank):
 
     e2e_loop(2)
     torch.cuda.synchronize()
+    copy_ev.clear()
     if world > 1:
         torch.distributed.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -302,6 +310,8 @@ def run_ours(args, rank, world, local_rank):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    # the input copies of the timed steps (the last one prefetches a step that is not run)
+    h2d_ms = statistics.mean(a.elapsed_time(b) for a, b in copy_ev[:args.steps])
 
     hbm, tflops, src = peaks()
     H, I = CFG["H"], CFG["I"]
@@ -326,7 +336,9 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"ep{world} (experts sharded, NCCL all-to-all)" if world > 1 else "single",
                    "l2": "working set (~1.5 GB int4 weights + activations) exceeds the 126 MB L2"},
         "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": UNIT,
-                "h2d_bytes_per_step": x.numel() * 2 + dy.numel() * 2, "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": x.numel() * 2 + dy.numel() * 2, "d2h_bytes_per_step": 4,
+                "ms_per_step": e2e_ms, "h2d_ms_per_step": h2d_ms,
+                "h2d_gbps": (x.numel() * 2 + dy.numel() * 2) / (h2d_ms * 1e-3) / 1e9},
         "roofline": {"bound": "tensor", "kernel": "usaf_expert_gate_up_fwd (grouped int4 GEMM + SwiGLU)",
                      "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
                      "frac": achieved / tflops, "peak_source": src, "kernel_ms": kern_ms,
