@@ -197,7 +197,8 @@ int usaf_expert_gate_up_bwd(const usaf_route_plan *plan, const usaf_qweight *w_g
  *   g = dtype( sum over expert e's slots s of gout[s, r] * gin[s, c] )
  *   compact[pos] += scale * g        (pos = compact position of the entry)
  * gout: [P, R] (dgu or dcur), gin: [P, C] (x_perm or h).
- * csr_to_compact: [n_ov] compact position of each CSR entry; scratch: fp32
+ * csr_to_compact: [n_ov] compact position of each CSR entry, or NULL when
+ * the compact vector is kept in CSR order (identity map); scratch: fp32
  * [n_ov] per-coordinate partial sums. */
 int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w, const void *gout,
                    const void *gin, int32_t dtype, const int32_t *csr_to_compact,
@@ -223,9 +224,10 @@ int usaf_sparse_dw_noalloc(const usaf_route_plan *plan, const usaf_qweight *w, c
  * compact mode: p = fp32 master [n]; m, v fp32 [n]; grad fp32 [n] (divided by
  * grad_div first, as train.py:662 divides by loss_scale*ACCUM).  Hyper-
  * parameters are doubles, converted the way Python scalars meet fp32 tensors.
- * If ov_val/ov_pos are given, the new value rounded the way the GEMMs consume
- * it (fp16, then `dtype`) is written to ov_val[ov_pos[i]] (and ov_valT[ov_posT[i]]),
- * as sync_resident does (usaf/moe_loader.py:425-443). */
+ * If ov_val is given, the new value rounded the way the GEMMs consume it
+ * (fp16, then `dtype`) is written to ov_val[ov_pos[i]] -- ov_val[i] when
+ * ov_pos is NULL (masters in CSR order) -- and to ov_valT[ov_posT[i]], as
+ * sync_resident does (usaf/moe_loader.py:425-443). */
 int usaf_sparse_adam(int64_t n, float *p, float *m, float *v, const float *grad,
                      double grad_div, int32_t step, double lr, double beta1, double beta2,
                      double eps, double weight_decay, int32_t dtype, float *ov_val,

@@ -60,7 +60,7 @@ __global__ void adam_compact_kernel(int64_t n, float *__restrict__ p, float *__r
         v[i] = vi;
         // the resident weight holds fp16(master) (usaf/moe_loader.py:442)
         float ev = to_f(from_f<Act>(__half2float(__float2half_rn(np))));
-        if (ov_val) ov_val[ov_pos[i]] = ev;
+        if (ov_val) ov_val[ov_pos ? ov_pos[i] : i] = ev;   // NULL map: CSR order
         if (ov_valT) ov_valT[ov_posT[i]] = ev;
     }
 }
@@ -96,7 +96,7 @@ extern "C" int usaf_sparse_adam(int64_t n, float *p, float *m, float *v, const f
     USAF_REQUIRE(n >= 0 && step >= 1);
     if (n == 0) return USAF_OK;
     USAF_REQUIRE(p && m && v && grad);
-    USAF_REQUIRE((ov_val == nullptr) == (ov_pos == nullptr));
+    USAF_REQUIRE(ov_val != nullptr || ov_pos == nullptr);
     USAF_REQUIRE((ov_valT == nullptr) == (ov_posT == nullptr));
     AdamConsts c = make_consts(step, lr, beta1, beta2, eps, weight_decay, grad_div);
     cudaStream_t st = as_stream(stream);

@@ -154,7 +154,7 @@ __global__ void __launch_bounds__(kThr) sddmm_kernel(usaf_route_plan pl, usaf_qw
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         for (int j = jb[h]; j < je[h]; ++j) {
-            const int pos = csr_to_compact[j];
+            const int pos = csr_to_compact ? csr_to_compact[j] : j;
             compact[pos] = __fadd_rn(compact[pos], __fmul_rn(scale, round_to<Act>(scratch[j])));
         }
     }
@@ -235,7 +235,7 @@ extern "C" int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w
                               float scale, float *compact, float *scratch, void *stream) {
     USAF_REQUIRE(plan && w && gout && gin);
     if (w->n_ov == 0) return USAF_OK;
-    USAF_REQUIRE(csr_to_compact && compact && scratch && w->row_ptr && w->col);
+    USAF_REQUIRE(compact && scratch && w->row_ptr && w->col);
     cudaStream_t st = as_stream(stream);
     if (dtype == USAF_BF16 && w->ov_mask && sddmm_tc_supported(w->R, w->C))
         return sddmm_tc_sparse(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin,

@@ -77,6 +77,11 @@ def kth_largest(vals: torch.Tensor, k: int) -> torch.Tensor:
     return out
 
 
+def _map(p) -> Optional[int]:
+    """csr -> compact map of a projection for the gradient kernels (NULL = identity)."""
+    return None if p.csr_identity else ptr(p.csr_to_compact)
+
+
 def _bitmap(words: torch.Tensor, bits: torch.Tensor, n_words: int) -> torch.Tensor:
     """int32 words with bit ``bits[i]`` of word ``words[i]`` set (pairs distinct)."""
     m = torch.zeros(n_words, dtype=torch.int64, device=words.device)
@@ -112,6 +117,7 @@ class Projection:
         self.row_ptr = self.col = self.val = None
         self.colT_ptr = self.rowT = self.valT = None
         self.csr_to_compact = self.compact_to_csr = self.compact_to_csc = None
+        self.csr_identity = False
         self.scratch = None
         self.ov_mask = None
         self.qT = self.szT = self.qP = None
@@ -163,6 +169,9 @@ class Projection:
         self.row_ptr = build_rowptr(k64 // Cc, E * R * 2)
         self.col = _i32(k64 % Cc)
         self.csr_to_compact = _i32(pcsr)
+        # compact vectors kept in CSR order (the layers do): the kernels take the
+        # identity map as NULL and stream instead of gathering
+        self.csr_identity = bool(torch.equal(pcsr, ar))
         self.compact_to_csr = torch.empty(n, dtype=torch.int32, device=dev)
         self.compact_to_csr[pcsr] = torch.arange(n, device=dev, dtype=torch.int32)
         # CSC: segments (column, half) with half = (row / 32) % 2, ascending row
@@ -366,10 +375,10 @@ class MoEBlock:
         st = stream()
         if gu.n_ov:
             call("usaf_sparse_dw", self.plan, gu.struct(), ptr(self.dgu), ptr(self.x_perm),
-                 self.dtc, ptr(gu.csr_to_compact), scale, ptr(compact_gu), ptr(gu.scratch), st)
+                 self.dtc, _map(gu), scale, ptr(compact_gu), ptr(gu.scratch), st)
         if dn.n_ov:
             call("usaf_sparse_dw", self.plan, dn.struct(), ptr(self.dcur), ptr(self.h),
-                 self.dtc, ptr(dn.csr_to_compact), scale, ptr(compact_dn), ptr(dn.scratch), st)
+                 self.dtc, _map(dn), scale, ptr(compact_dn), ptr(dn.scratch), st)
 
     def dense_abs_grad(self, which: str) -> torch.Tensor:
         """|dW| of every expert of one projection as fp32 [E, R, C] (importance)."""
@@ -410,7 +419,7 @@ def sparse_adam_compact(master, m, v, grad, step, lr, betas, eps, weight_decay, 
          int(step), float(lr), float(betas[0]), float(betas[1]), float(eps),
          float(weight_decay), _lib.dtype_code(dtype),
          ptr(proj.val) if proj is not None else None,
-         ptr(proj.compact_to_csr) if proj is not None else None,
+         None if proj is None or proj.csr_identity else ptr(proj.compact_to_csr),
          ptr(proj.valT) if proj is not None else None,
          ptr(proj.compact_to_csc) if proj is not None else None, stream())
 

@@ -25,7 +25,7 @@ import torch.distributed as dist
 
 from . import _lib
 from ._lib import call, ptr, stream
-from .engine import BlockDims, MoEBlock, Projection
+from .engine import BlockDims, MoEBlock, Projection, _map
 from .moe_loader import SparseGradStore, TopKImportanceStore, select_candidates
 from .sparse_optim import SparseAdam
 
@@ -237,10 +237,10 @@ class ExpertParallelMoE:
         st = stream()
         if self.gu.n_ov:
             call("usaf_sparse_dw", self.own, self.gu.struct(), ptr(self.dgu_own), ptr(self.x_own),
-                 self.dtc, ptr(self.gu.csr_to_compact), scale, ptr(compact_gu), ptr(self.gu.scratch), st)
+                 self.dtc, _map(self.gu), scale, ptr(compact_gu), ptr(self.gu.scratch), st)
         if self.dn.n_ov:
             call("usaf_sparse_dw", self.own, self.dn.struct(), ptr(self.dcur_own), ptr(self.h_own),
-                 self.dtc, ptr(self.dn.csr_to_compact), scale, ptr(compact_dn), ptr(self.dn.scratch), st)
+                 self.dtc, _map(self.dn), scale, ptr(compact_dn), ptr(self.dn.scratch), st)
 
     def dense_abs_grad(self, which: str) -> torch.Tensor:
         """|dW| of this rank's experts (fp32 [El, R, C]) for the importance pass."""
