@@ -26,6 +26,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -72,7 +73,9 @@ class ClockSampler:
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu}.csv")
+        # raw samples: $USAF_CLOCKS_DIR (to keep them) or the temp directory
+        out_dir = os.environ.get("USAF_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"clocks_gpu{gpu}.csv")
         self.t0 = self.t1 = None
 
     def __enter__(self):
