@@ -352,17 +352,26 @@ __global__ void sddmm_accumulate(int n, const float *__restrict__ g, const int32
     }
 }
 
-// the same when compact is in CSR order (identity map): 16-byte vectors, n4 = n / 4
-__global__ void sddmm_accumulate_id(int n4, const float4 *__restrict__ g, float scale,
-                                    float4 *__restrict__ compact) {
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n4; j += gridDim.x * blockDim.x) {
-        const float4 a = g[j];
-        float4 c = compact[j];
+// the same when compact is in CSR order (identity map): 16-byte vectors for the
+// first n / 4 * 4 entries, the last n % 4 by the first threads
+__global__ void sddmm_accumulate_id(int n, const float *__restrict__ g, float scale,
+                                    float *__restrict__ compact) {
+    const int n4 = n / 4;
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    float4 *c4 = reinterpret_cast<float4 *>(compact);
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+    for (int j = tid; j < n4; j += gridDim.x * blockDim.x) {
+        const float4 a = g4[j];
+        float4 c = c4[j];
         c.x = __fadd_rn(c.x, __fmul_rn(scale, a.x));
         c.y = __fadd_rn(c.y, __fmul_rn(scale, a.y));
         c.z = __fadd_rn(c.z, __fmul_rn(scale, a.z));
         c.w = __fadd_rn(c.w, __fmul_rn(scale, a.w));
-        compact[j] = c;
+        c4[j] = c;
+    }
+    if (tid < n - n4 * 4) {
+        const int j = n4 * 4 + tid;
+        compact[j] = __fadd_rn(compact[j], __fmul_rn(scale, g[j]));
     }
 }
 
@@ -437,11 +446,11 @@ int sddmm_tc_sparse(const usaf_route_plan *pl, const usaf_qweight *w, const __nv
     int rc = sddmm_tc_launch<EPI_SPARSE>(pl, w->R, w->C, gout, gin, w->row_ptr, w->ov_mask, scratch, st);
     if (rc != USAF_OK) return rc;
     const int n = w->n_ov;
-    if (!c2c && n % 4 == 0 && !((uintptr_t)scratch & 15) && !((uintptr_t)compact & 15)) {
+    if (!c2c && !((uintptr_t)scratch & 15) && !((uintptr_t)compact & 15)) {
         const int n4 = n / 4;
-        sddmm_accumulate_id<<<std::min((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(
-            n4, reinterpret_cast<const float4 *>(scratch), scale, reinterpret_cast<float4 *>(compact));
-    } else {   // a compact map, or an identity map on ragged / unaligned buffers
+        sddmm_accumulate_id<<<std::max(1, std::min((n4 + 255) / 256, 148 * 8)), 256, 0, st>>>(n, scratch, scale,
+                                                                                             compact);
+    } else {   // a compact map, or an identity map on unaligned buffers
         sddmm_accumulate<<<std::min((n + 255) / 256, 148 * 16), 256, 0, st>>>(n, scratch, c2c, scale, compact);
     }
     USAF_CHECK_LAUNCH();
