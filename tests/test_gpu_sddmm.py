@@ -87,9 +87,11 @@ def check(got, ref, what):
 
 
 CASES = [
-    dict(T=256, H=512, E=32, k=4, I=384, zipf=1.5, seed=3, skew=True),     # C % 256 == 128 tiles
-    dict(T=40, H=512, E=16, k=2, I=256, zipf=0.0, seed=4, skew=False),     # every expert < 64 slots
+    # the first three run the tensor-core kernel (pair capacity above 64 per expert)
+    dict(T=320, H=512, E=32, k=4, I=384, zipf=1.5, seed=3, skew=True),     # C % 256 == 128 tiles
+    dict(T=320, H=512, E=16, k=2, I=256, zipf=0.0, seed=4, skew=False),    # experts of ~40 slots (< 64)
     dict(T=1024, H=2048, E=128, k=8, I=768, zipf=1.2, seed=5, skew=True),  # Qwen3-30B-A3B shapes
+    dict(T=8, H=512, E=32, k=4, I=384, zipf=0.0, seed=6, skew=True),       # decode-sized: CUDA-core path
 ]
 
 

@@ -28,6 +28,16 @@ namespace usaf {
 static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 static inline unsigned cdiv(int64_t a, int64_t b) { return (unsigned)((a + b - 1) / b); }
 
+// Plans whose pair capacity is at most this many pairs per expert (about half
+// of it routed: batches of up to ~32 tokens per expert) take the CUDA-core
+// expert-weight gradient kernel: the tensor-core SDDMM spends a fixed cost
+// per 128 x 256 tile whatever the expert's slot count (C2 layer, measured:
+// T = 256 459 -> 225 us, T = 512 460 -> 280 us, T = 1 213 -> 74 us).
+constexpr int kSimtMaxPairsPerExpert = 64;
+static inline bool small_plan(const usaf_route_plan *pl) {
+    return (int64_t)pl->P_cap <= (int64_t)kSimtMaxPairsPerExpert * pl->E;
+}
+
 // ---- activation dtype plumbing -------------------------------------------
 // Values move through fp32 registers; `Act` is the storage type.
 __device__ __forceinline__ float to_f(float v) { return v; }

@@ -237,12 +237,21 @@ extern "C" int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w
     if (w->n_ov == 0) return USAF_OK;
     USAF_REQUIRE(compact && scratch && w->row_ptr && w->col);
     cudaStream_t st = as_stream(stream);
-    if (dtype == USAF_BF16 && w->ov_mask && sddmm_tc_supported(w->R, w->C))
+    const bool tc = dtype == USAF_BF16 && w->ov_mask && sddmm_tc_supported(w->R, w->C);
+    if (tc && !small_plan(plan))
         return sddmm_tc_sparse(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin,
                                csr_to_compact, scale, compact, scratch, st);
     switch (dtype) {
         case USAF_F32: return sddmm_launch<float>(plan, w, (const float *)gout, (const float *)gin, csr_to_compact, scale, compact, scratch, st);
-        case USAF_BF16: return sddmm_launch<__nv_bfloat16>(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin, csr_to_compact, scale, compact, scratch, st);
+        case USAF_BF16: {
+            // a few slots per expert: the CUDA-core kernel, which skips experts without
+            // slots (it stages all C columns, so wide projections stay on tensor cores)
+            const int rc = sddmm_launch<__nv_bfloat16>(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin, csr_to_compact, scale, compact, scratch, st);
+            if (rc == USAF_EUNSUPPORTED && tc)
+                return sddmm_tc_sparse(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin,
+                                       csr_to_compact, scale, compact, scratch, st);
+            return rc;
+        }
         default: return USAF_EINVAL;
     }
 }
