@@ -199,7 +199,10 @@ int usaf_expert_gate_up_bwd(const usaf_route_plan *plan, const usaf_qweight *w_g
  * gout: [P, R] (dgu or dcur), gin: [P, C] (x_perm or h).
  * csr_to_compact: [n_ov] compact position of each CSR entry, or NULL when
  * the compact vector is kept in CSR order (identity map); scratch: fp32
- * [n_ov] per-coordinate partial sums. */
+ * [n_ov] per-coordinate partial sums.  bf16 with w->ov_mask runs on the
+ * tensor cores unless the plan holds at most 64 pair slots per expert
+ * (P_cap <= 64 * E, decode-sized batches), which take the CUDA-core kernel;
+ * the results agree to bf16 rounding. */
 int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w, const void *gout,
                    const void *gin, int32_t dtype, const int32_t *csr_to_compact,
                    float scale, float *compact, float *scratch, void *stream);
