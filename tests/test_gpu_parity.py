@@ -15,7 +15,7 @@ import torch
 
 from oracle import moe as omoe
 from oracle import quant as oquant
-from oracle.flow import PREFIX, run_step
+from oracle.flow import PREFIX
 from oracle.inputs import C1, make_block_inputs
 
 pytestmark = pytest.mark.gpu

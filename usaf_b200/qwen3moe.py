@@ -29,7 +29,7 @@ The router weight receives its gradient through autograd.
 """
 from __future__ import annotations
 
-from typing import Dict, Optional, Tuple
+from typing import Dict, Tuple
 
 import torch
 
