@@ -179,7 +179,9 @@ int usaf_gather_dx(const usaf_route_plan *plan, const void *dx_seg, const float 
  *       (gu: [P, 2I], h: [P, I], activation dtype, rounded like the reference)
  *   usaf_expert_down_fwd:    y_seg = h @ W_dn[e]^T              ([P, H])
  *   usaf_expert_down_bwd:    dh = dcur @ W_dn[e]; dgu = SwiGLU backward(dh, gu)
- *   usaf_expert_gate_up_bwd: dx_seg = dgu @ W_gu[e]             ([P, H]) */
+ *   usaf_expert_gate_up_bwd: dx_seg = dgu @ W_gu[e]             ([P, H])
+ * plan->E must equal the projection's E (USAF_EINVAL otherwise); the
+ * tensor-core kernels take E <= 1024. */
 int usaf_expert_gate_up_fwd(const usaf_route_plan *plan, const usaf_qweight *w_gu,
                             const void *x_perm, int32_t dtype, void *gu, void *h, void *stream);
 int usaf_expert_down_fwd(const usaf_route_plan *plan, const usaf_qweight *w_dn,

@@ -26,7 +26,7 @@ static bool qweight_ok(const usaf_qweight *w) {
 extern "C" int usaf_expert_gate_up_fwd(const usaf_route_plan *plan, const usaf_qweight *w_gu,
                                        const void *x_perm, int32_t dtype, void *gu, void *h,
                                        void *stream) {
-    USAF_REQUIRE(plan && qweight_ok(w_gu) && x_perm && gu && h && w_gu->R % 2 == 0);
+    USAF_REQUIRE(plan && qweight_ok(w_gu) && x_perm && gu && h && w_gu->R % 2 == 0 && plan->E == w_gu->E);
     cudaStream_t st = as_stream(stream);
     const int K = w_gu->C, N = w_gu->R, I = N / 2;
     int rc;
@@ -46,7 +46,7 @@ extern "C" int usaf_expert_gate_up_fwd(const usaf_route_plan *plan, const usaf_q
 
 extern "C" int usaf_expert_down_fwd(const usaf_route_plan *plan, const usaf_qweight *w_dn,
                                     const void *h, int32_t dtype, void *y_seg, void *stream) {
-    USAF_REQUIRE(plan && qweight_ok(w_dn) && h && y_seg);
+    USAF_REQUIRE(plan && qweight_ok(w_dn) && h && y_seg && plan->E == w_dn->E);
     cudaStream_t st = as_stream(stream);
     const int K = w_dn->C, N = w_dn->R;
     if (dtype == USAF_F32) return launch_simt<float, false>(plan, w_dn, (const float *)h, K, N, (float *)y_seg, N, st);
@@ -60,7 +60,7 @@ extern "C" int usaf_expert_down_fwd(const usaf_route_plan *plan, const usaf_qwei
 extern "C" int usaf_expert_down_bwd(const usaf_route_plan *plan, const usaf_qweight *w_dn,
                                     const void *dcur, const void *gu, int32_t dtype, void *dgu,
                                     void *stream) {
-    USAF_REQUIRE(plan && qweight_ok(w_dn) && dcur && gu && dgu);
+    USAF_REQUIRE(plan && qweight_ok(w_dn) && dcur && gu && dgu && plan->E == w_dn->E);
     USAF_REQUIRE(w_dn->n_ov == 0 || (w_dn->colT_ptr && w_dn->rowT && w_dn->valT));
     cudaStream_t st = as_stream(stream);
     // dh = dcur @ W_dn[e] (storage [E,H,I]: K = H = R, N = I = C), written
@@ -84,7 +84,7 @@ extern "C" int usaf_expert_down_bwd(const usaf_route_plan *plan, const usaf_qwei
 extern "C" int usaf_expert_gate_up_bwd(const usaf_route_plan *plan, const usaf_qweight *w_gu,
                                        const void *dgu, int32_t dtype, void *dx_seg,
                                        void *stream) {
-    USAF_REQUIRE(plan && qweight_ok(w_gu) && dgu && dx_seg);
+    USAF_REQUIRE(plan && qweight_ok(w_gu) && dgu && dx_seg && plan->E == w_gu->E);
     USAF_REQUIRE(w_gu->n_ov == 0 || (w_gu->colT_ptr && w_gu->rowT && w_gu->valT));
     cudaStream_t st = as_stream(stream);
     // dx = dgu @ W_gu[e] (storage [E,2I,H]: K = 2I = R, N = H = C)

@@ -233,7 +233,7 @@ using namespace usaf;
 extern "C" int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w, const void *gout,
                               const void *gin, int32_t dtype, const int32_t *csr_to_compact,
                               float scale, float *compact, float *scratch, void *stream) {
-    USAF_REQUIRE(plan && w && gout && gin);
+    USAF_REQUIRE(plan && w && gout && gin && plan->E == w->E);
     if (w->n_ov == 0) return USAF_OK;
     USAF_REQUIRE(compact && scratch && w->row_ptr && w->col);
     cudaStream_t st = as_stream(stream);
