@@ -1,6 +1,7 @@
 """Host logic of expert parallelism on CPU with the gloo backend (world size
-2 and 4): count exchange, split sizes, the all-to-all of rows to the experts'
-owners in expert-major order and the way back.  The regrouping uses the
+2, 3 and 4, and a rank that routes no rows at all): count exchange, split
+sizes, the all-to-all of rows to the experts' owners in expert-major order
+and the way back.  The regrouping uses the
 reference index arithmetic of tests/ep_reference.py (the device kernel is
 checked against the same arithmetic in tests/test_gpu_ep.py)."""
 import os
@@ -20,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, E, H, q):
+def _worker(rank, world, port, E, H, q, empty_rank=-1):
     try:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                                 world_size=world)
@@ -32,6 +33,8 @@ def _worker(rank, world, port, E, H, q):
         g = torch.Generator().manual_seed(100 + rank)
         cnt = torch.randint(0, 6, (E,), generator=g, dtype=torch.int32)
         cnt[rank] = 0                                   # an expert without rows
+        if rank == empty_rank:
+            cnt.zero_()                                 # this rank routes nothing
         # expert-major rows of this rank: value = (rank, expert, index, column)
         rows = []
         for e in range(E):
@@ -63,12 +66,12 @@ def _worker(rank, world, port, E, H, q):
         q.put((rank, repr(e)))
 
 
-@pytest.mark.parametrize("world,E", [(2, 8), (4, 16)])
-def test_exchange_roundtrip_gloo(world, E):
+@pytest.mark.parametrize("world,E,empty_rank", [(2, 8, -1), (3, 12, -1), (4, 16, -1), (2, 8, 1)])
+def test_exchange_roundtrip_gloo(world, E, empty_rank):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, E, 3, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, E, 3, q, empty_rank)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=240) for _ in range(world))
