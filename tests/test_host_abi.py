@@ -45,3 +45,41 @@ def test_cpu_tensor_rejected():
     from usaf_b200 import _lib
     with pytest.raises(TypeError):
         _lib.ptr(torch.zeros(3))
+
+
+def _prototypes():
+    src = open(HDR).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(usaf_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src):
+        args = m.group(2).strip()
+        out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_binding_arity_matches_header():
+    """Every ctypes signature takes as many arguments as the C prototype."""
+    from usaf_b200 import _lib
+    protos = _prototypes()
+    bad = {n: (protos[n], len(_lib._SIGS[n][1])) for n in protos
+           if n in _lib._SIGS and protos[n] != len(_lib._SIGS[n][1])}
+    assert not bad, bad
+
+
+def _struct_fields(name):
+    src = open(HDR).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    end = re.search(r"\}\s*" + name + r"\s*;", src).start()
+    body = src[src.rindex("typedef struct {", 0, end) + len("typedef struct {"):end]
+    n = 0
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if decl:
+            n += decl.count(",") + 1     # "int32_t T, E, P_cap" declares three
+    return n
+
+
+def test_struct_layouts_match_header():
+    from usaf_b200 import _lib
+    assert len(_lib.QWeight._fields_) == _struct_fields("usaf_qweight")
+    assert len(_lib.RoutePlan._fields_) == _struct_fields("usaf_route_plan")
