@@ -82,6 +82,17 @@ def _map(p) -> Optional[int]:
     return None if p.csr_identity else ptr(p.csr_to_compact)
 
 
+def _check_act(name: str, t: torch.Tensor, shape, dtype: torch.dtype):
+    """Shape / dtype / layout check of a tensor handed to the kernels: a wrong
+    size would make them read or write past the buffer, so it raises here."""
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name}: expected shape {tuple(shape)}, got {tuple(t.shape)}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name}: expected dtype {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: must be contiguous")
+
+
 def _bitmap(words: torch.Tensor, bits: torch.Tensor, n_words: int) -> torch.Tensor:
     """int32 words with bit ``bits[i]`` of word ``words[i]`` set (pairs distinct)."""
     m = torch.zeros(n_words, dtype=torch.int64, device=words.device)
@@ -106,6 +117,17 @@ class Projection:
             raise ValueError("int4 groups must not straddle rows (C % group_size != 0)")
         if 2 * E * R * Cc >= 2 ** 32:
             raise ValueError("projection too large for 32-bit overlay keys")
+        n_el = E * R * Cc
+        # the usaf.quantization layout: 2 codes per byte, one fp16 scale and zero per group
+        if q.numel() * 2 != n_el or q.dtype not in (torch.int8, torch.uint8):
+            raise ValueError(f"q: expected {n_el // 2} int8 bytes for shape {tuple(shape)}, "
+                             f"got {q.numel()} {q.dtype}")
+        for nm, t in (("s", s), ("z", z)):
+            if t.numel() != n_el // group_size or t.dtype != torch.float16:
+                raise ValueError(f"{nm}: expected {n_el // group_size} fp16 values, "
+                                 f"got {t.numel()} {t.dtype}")
+        if not (q.device == s.device == z.device):
+            raise ValueError("q, s and z must be on the same device")
         self.E, self.R, self.C, self.group_size = E, R, Cc, group_size
         self.shape = (E, R, Cc)
         self.q = q.reshape(-1).contiguous()
@@ -153,7 +175,10 @@ class Projection:
         dev = self.device
         idx = idx.reshape(-1).to(device=dev, dtype=torch.int64)
         n = idx.numel()
-        self.n_ov = n
+        if master.numel() != n:
+            raise ValueError(f"{master.numel()} master values for {n} overlay coordinates")
+        if n and (int(idx.min()) < 0 or int(idx.max()) >= self.numel()):
+            raise ValueError(f"overlay index out of range [0, {self.numel()})")
         E, R, Cc = self.E, self.R, self.C
         ar = torch.arange(n, device=dev, dtype=torch.int64)
         M32 = 0xFFFFFFFF
@@ -165,6 +190,9 @@ class Projection:
         # threads per row, each walking its own sorted segment
         key = ((e * R + r) * 2 + ((c >> 5) & 1)) * Cc + c
         kcsr, pcsr = sort_u32(key, ar)
+        if n > 1 and bool((kcsr[1:] == kcsr[:-1]).any()):
+            raise ValueError("duplicate overlay coordinates")
+        self.n_ov = n
         k64 = kcsr.to(torch.int64) & M32
         self.row_ptr = build_rowptr(k64 // Cc, E * R * 2)
         self.col = _i32(k64 % Cc)
@@ -293,7 +321,8 @@ class MoEBlock:
     # ---------------------------------------------------------------- fwd ---
     def forward(self, x: torch.Tensor, w_r: torch.Tensor, gu: Projection, dn: Projection):
         d = self.d
-        assert x.shape == (d.T, d.H) and x.dtype == self.dt and x.is_contiguous()
+        _check_act("x", x, (d.T, d.H), self.dt)
+        _check_act("w_r", w_r, (d.E, d.H), self.dt)
         st = stream()
         call("usaf_router_fwd", ptr(x), ptr(w_r), self.dtc, d.T, d.H, d.E, d.top_k,
              int(d.norm_topk_prob), ptr(self.logits), ptr(self.probs), ptr(self.wsum),
@@ -311,7 +340,9 @@ class MoEBlock:
     def backward(self, dy: torch.Tensor, x: torch.Tensor, w_r: torch.Tensor, gu: Projection,
                  dn: Projection):
         d = self.d
-        assert dy.shape == (d.T, d.H) and dy.dtype == self.dt and dy.is_contiguous()
+        _check_act("dy", dy, (d.T, d.H), self.dt)
+        _check_act("x", x, (d.T, d.H), self.dt)
+        _check_act("w_r", w_r, (d.E, d.H), self.dt)
         st = stream()
         call("usaf_combine_bwd", self.plan, ptr(dy), ptr(self.y_seg), self.dtc, d.H,
              ptr(self.dcur), ptr(self.dw_pair), st)
@@ -334,8 +365,8 @@ class MoEBlock:
         gives (nonzero = routed), as ``dml_qwen3_experts_forward``
         (usaf/qwen3moe_dml.py:24-64) receives them."""
         d = self.d
-        assert x.shape == (d.T, d.H) and x.dtype == self.dt and x.is_contiguous()
-        assert weights.shape == (d.T, d.E) and weights.dtype == self.dt and weights.is_contiguous()
+        _check_act("x", x, (d.T, d.H), self.dt)
+        _check_act("weights", weights, (d.T, d.E), self.dt)
         st = stream()
         self.weights.copy_(weights)
         call("usaf_dispatch", self.plan, ptr(self.weights), ptr(x), self.dtc, d.H,
@@ -350,7 +381,7 @@ class MoEBlock:
     def experts_backward(self, dy: torch.Tensor, gu: Projection, dn: Projection):
         """Backward of :meth:`experts_forward`: (dX [T, H], dweights [T, E])."""
         d = self.d
-        assert dy.shape == (d.T, d.H) and dy.dtype == self.dt and dy.is_contiguous()
+        _check_act("dy", dy, (d.T, d.H), self.dt)
         st = stream()
         call("usaf_combine_bwd", self.plan, ptr(dy), ptr(self.y_seg), self.dtc, d.H,
              ptr(self.dcur), ptr(self.dw_pair), st)
@@ -372,6 +403,9 @@ class MoEBlock:
     def sparse_grads(self, gu: Projection, dn: Projection, compact_gu: torch.Tensor,
                      compact_dn: torch.Tensor, scale: float = 1.0):
         """compact[pos] += scale * dtype(dW[e,r,c]) at every overlay coordinate."""
+        for nm, p, c in (("compact_gu", gu, compact_gu), ("compact_dn", dn, compact_dn)):
+            if p.n_ov:
+                _check_act(nm, c, (p.n_ov,), torch.float32)
         st = stream()
         if gu.n_ov:
             call("usaf_sparse_dw", self.plan, gu.struct(), ptr(self.dgu), ptr(self.x_perm),
@@ -415,6 +449,10 @@ def sparse_adam_compact(master, m, v, grad, step, lr, betas, eps, weight_decay, 
     """One fused SparseAdam step (usaf/sparse_optim.py:86-134, compact mode),
     writing the new overlay values of ``proj`` (sync_resident) in the same pass."""
     n = master.numel()
+    for nm, t in (("master", master), ("m", m), ("v", v), ("grad", grad)):
+        _check_act(nm, t, (n,), torch.float32)
+    if proj is not None and proj.n_ov != n:
+        raise ValueError(f"{n} masters for an overlay of {proj.n_ov} coordinates")
     call("usaf_sparse_adam", n, ptr(master), ptr(m), ptr(v), ptr(grad), float(grad_div),
          int(step), float(lr), float(betas[0]), float(betas[1]), float(eps),
          float(weight_decay), _lib.dtype_code(dtype),
@@ -429,6 +467,12 @@ def sparse_adam_gather(param, grad, idx, m, v, step, lr, betas, eps, weight_deca
     """SparseAdam gather/scatter mode (usaf/sparse_optim.py:110-134) on a
     dense parameter (the router)."""
     n = idx.numel()
+    for nm, t in (("m", m), ("v", v)):
+        _check_act(nm, t, (n,), torch.float32)
+    if idx.dtype != torch.int64 or not idx.is_contiguous():
+        raise TypeError("idx: contiguous int64 expected")
+    if grad.numel() != param.numel() or grad.dtype != param.dtype or not grad.is_contiguous():
+        raise ValueError("grad: a contiguous tensor of the parameter's size and dtype expected")
     call("usaf_sparse_adam_gather", n, ptr(idx), ptr(param), ptr(grad),
          _lib.dtype_code(param.dtype), float(grad_div), ptr(m), ptr(v), int(step), float(lr),
          float(betas[0]), float(betas[1]), float(eps), float(weight_decay), stream())

@@ -25,7 +25,7 @@ import torch.distributed as dist
 
 from . import _lib
 from ._lib import call, ptr, stream
-from .engine import BlockDims, MoEBlock, Projection, _map
+from .engine import BlockDims, MoEBlock, Projection, _check_act, _map
 from .moe_loader import SparseGradStore, TopKImportanceStore, select_candidates
 from .sparse_optim import SparseAdam
 
@@ -177,7 +177,8 @@ class ExpertParallelMoE:
     # ---------------------------------------------------------------- fwd ---
     def forward(self, x: torch.Tensor, w_r: torch.Tensor) -> torch.Tensor:
         s, d = self.src, self.src.d
-        assert x.shape == (d.T, d.H) and x.dtype == self.dt and x.is_contiguous()
+        _check_act("x", x, (d.T, d.H), self.dt)
+        _check_act("w_r", w_r, (d.E, d.H), self.dt)
         st = stream()
         call("usaf_router_fwd", ptr(x), ptr(w_r), self.dtc, d.T, d.H, d.E, d.top_k,
              int(d.norm_topk_prob), ptr(s.logits), ptr(s.probs), ptr(s.wsum), ptr(s.weights),
@@ -206,7 +207,9 @@ class ExpertParallelMoE:
         dX rows travel back, and the router backward runs while the output
         gradients travel to the owners."""
         s, d, xp = self.src, self.src.d, self.xp
-        assert dy.shape == (d.T, d.H) and dy.dtype == self.dt and dy.is_contiguous()
+        _check_act("dy", dy, (d.T, d.H), self.dt)
+        _check_act("x", x, (d.T, d.H), self.dt)
+        _check_act("w_r", w_r, (d.E, d.H), self.dt)
         st = stream()
         call("usaf_combine_bwd", s.plan, ptr(dy), ptr(s.y_seg), self.dtc, d.H, ptr(s.dcur),
              ptr(s.dw_pair), st)

@@ -42,13 +42,24 @@ class SparseAdam:
             raise TypeError("usaf_b200 SparseAdam keeps its state on the parameter's CUDA device")
         return p.device
 
+    def _check_idx(self, name, idx):
+        """The kernels index the parameter (gather/scatter mode) or its gradient
+        with ``idx``; an entry outside them is refused here, where the
+        reference's own torch indexing would raise IndexError in ``step``."""
+        lo, hi = int(idx.min()), int(idx.max())
+        if lo < 0 or (not self.compact_params and hi >= self._named[name].numel()):
+            raise IndexError(f"{name}: active index out of range")
+        self._idx_max[name] = hi
+
     def _build_state_from_idx(self, active_idx):
         self._active_ids, self._idx, self._m, self._v = [], {}, {}, {}
+        self._idx_max: Dict[str, int] = {}
         for name, idx in active_idx.items():
             if name not in self._named or idx is None or idx.numel() == 0:
                 continue
             dev = self._dev(name)
             idx = idx.reshape(-1).to(device=dev, dtype=torch.long)
+            self._check_idx(name, idx)
             self._active_ids.append(name)
             self._idx[name] = idx
             self._m[name] = torch.zeros(idx.numel(), device=dev, dtype=torch.float32)
@@ -56,6 +67,7 @@ class SparseAdam:
 
     def _build_state(self, active_mask):
         self._active_ids, self._idx, self._m, self._v = [], {}, {}, {}
+        self._idx_max: Dict[str, int] = {}
         for name in self._named:
             mask = active_mask.get(name)
             if mask is None:
@@ -64,6 +76,7 @@ class SparseAdam:
             idx = mask.reshape(-1).to(device=dev, dtype=torch.bool).nonzero().reshape(-1)
             if idx.numel() == 0:
                 continue
+            self._check_idx(name, idx)
             self._active_ids.append(name)
             self._idx[name] = idx
             self._m[name] = torch.zeros(idx.numel(), device=dev, dtype=torch.float32)
@@ -109,6 +122,8 @@ class SparseAdam:
                 grad = dense
             else:
                 grad = p.grad.detach().reshape(-1).contiguous()
+                if self._idx_max[name] >= grad.numel():
+                    raise IndexError(f"{name}: active index out of range of its gradient")
             if self.compact_params:
                 engine.sparse_adam_compact(p.data, self._m[name], self._v[name],
                                            grad.float().index_select(0, self._idx[name]),
@@ -138,10 +153,10 @@ class SparseAdam:
         self._step = int(sd["step"])
         for n, t in sd["m"].items():
             if n in self._m and t.numel() == self._m[n].numel():
-                self._m[n] = t.detach().to(self._m[n].device).float().clone()
+                self._m[n] = t.detach().reshape(-1).to(self._m[n].device).float().clone()
         for n, t in sd["v"].items():
             if n in self._v and t.numel() == self._v[n].numel():
-                self._v[n] = t.detach().to(self._v[n].device).float().clone()
+                self._v[n] = t.detach().reshape(-1).to(self._v[n].device).float().clone()
 
     @property
     def num_active_params(self) -> int:
