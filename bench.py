@@ -555,15 +555,19 @@ def run_c5(steps: int = 10, warmup: int = 3):
                       "steps": steps, "warmup": warmup, "data": "synthetic"}), flush=True)
 
 
-def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2):
-    """BASELINE configs[2] (C3) on one GPU at a reduced depth: a random-init
-    Qwen3MoeForCausalLM with the C3 layer shapes (H 2048, 32/4 heads, head dim
-    128, E 128, top-8, I 768, vocab 151936), int4 g128 experts attached through
-    patch_qwen3moe_for_b200, sequence 2048 x micro-batch 4, LM cross-entropy,
-    trained by usaf_b200.trainer.SparseTrainer (importance pass, 0.5 %
-    selection, loss scaling, SparseAdam + SGD-momentum router).  Attention,
-    norms, embeddings and the LM head run in PyTorch; one JSON line with the
-    whole-model tokens/s and the per-layer time."""
+def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2, recompute: bool = True):
+    """BASELINE configs[2] (C3) on one GPU: a random-init Qwen3MoeForCausalLM
+    with the C3 shapes (H 2048, 32/4 heads, head dim 128, E 128, top-8, I 768,
+    vocab 151936) at ``n_layers`` of its 48 layers, int4 g128 experts attached
+    through patch_qwen3moe_for_b200, sequence 2048 x micro-batch 4, LM
+    cross-entropy, trained by usaf_b200.trainer.SparseTrainer (importance
+    pass, 0.5 % selection, loss scaling, SparseAdam + SGD-momentum router).
+    Attention, norms, embeddings and the LM head run in PyTorch.  Memory for
+    the full depth: the experts are built without dense weights, the blocks
+    share their backward-only buffers, the pair buffers hold 1.25 x top_k
+    pairs per token, and (``recompute``, as the reference's loader enables,
+    usaf/moe_loader.py:758-760) each decoder layer's activations are
+    recomputed in the backward.  One JSON line with the whole-model tokens/s."""
     from transformers.models.qwen3_moe.configuration_qwen3_moe import Qwen3MoeConfig
     from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeForCausalLM
     from usaf_b200 import qwen3moe
@@ -573,16 +577,20 @@ def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     qwen3moe.patch_qwen3moe_for_b200()
+    qwen3moe.configure_workspaces(pair_factor=1.25, share_backward=True)
     H, E, k, I, V, S, MB = 2048, 128, 8, 768, 151936, 2048, 4
     cfg = Qwen3MoeConfig(vocab_size=V, hidden_size=H, intermediate_size=6144, num_hidden_layers=n_layers,
                          num_attention_heads=32, num_key_value_heads=4, head_dim=128,
                          moe_intermediate_size=I, num_experts=E, num_experts_per_tok=k,
                          norm_topk_prob=True, max_position_embeddings=4096)
     torch.manual_seed(3)
-    with torch.device(dev):
+    with torch.device(dev), qwen3moe.without_dense_experts():
         model = Qwen3MoeForCausalLM(cfg).to(torch.bfloat16)
     for p_ in model.parameters():
         p_.requires_grad_(False)
+    if recompute:
+        model.gradient_checkpointing_enable(gradient_checkpointing_kwargs={"use_reentrant": False})
+    model.train()
     g = torch.Generator(device=dev).manual_seed(3)
     for layer in model.model.layers:
         mlp = layer.mlp
@@ -593,9 +601,6 @@ def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2):
             q, s_, z, _ = quantize_4bit(w, 128)
             del w
             ps.append(Projection(q, s_, z, shape, 128, torch.bfloat16))
-        # the module's own expert tensors are not read by the patched forward
-        mlp.experts.gate_up_proj = torch.nn.Parameter(torch.empty(0, device=dev), requires_grad=False)
-        mlp.experts.down_proj = torch.nn.Parameter(torch.empty(0, device=dev), requires_grad=False)
         qwen3moe.attach_int4_experts(mlp.experts, *ps)
     gt = torch.Generator(device=dev).manual_seed(4)
     batches = [torch.randint(0, V, (MB, S), device=dev, generator=gt) for _ in range(2)]
@@ -615,7 +620,9 @@ def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2):
                       "(C3 layer shapes), seq 2048 x mb 4, LM cross-entropy, int4 experts, 0.5% sparse, "
                       "SparseTrainer steps", "layers": n_layers, "tokens_per_step": MB * S,
                       "step_ms": ms, "tokens_per_s": MB * S / (ms * 1e-3),
-                      "ms_per_layer_incl_head": ms / n_layers, "losses": [round(l_["loss"], 4) for l_ in logs],
+                      "ms_per_layer_incl_head": ms / n_layers, "activation_recompute": recompute,
+                      "max_memory_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
+                      "losses": [round(l_["loss"], 4) for l_ in logs],
                       "all_finite": all(l_["finite"] for l_ in logs), "steps": steps, "warmup": warmup,
                       "data": "synthetic (uniform token ids)"}), flush=True)
 
@@ -644,6 +651,8 @@ def main():
                     help="Mixtral-8x22B-shaped layer: importance pass + sparse steps (1 GPU)")
     ap.add_argument("--c3", type=int, default=0, metavar="LAYERS",
                     help="C3-shaped causal LM with this many layers through SparseTrainer (1 GPU)")
+    ap.add_argument("--c3-no-recompute", action="store_true",
+                    help="keep every decoder layer's activations instead of recomputing them")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -654,7 +663,7 @@ def main():
         run_c5()
         return
     if args.c3:
-        run_c3(args.c3)
+        run_c3(args.c3, recompute=not args.c3_no_recompute)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

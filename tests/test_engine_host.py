@@ -73,3 +73,46 @@ def test_block_workspace_needs_a_device():
                             dtype=torch.bfloat16)
     with pytest.raises(TypeError):
         engine.MoEBlock(dims, "cpu")
+
+
+def test_pair_capacity():
+    assert engine.pair_capacity(4096, 128, 8) == 4096 * 16           # default: room for 2 x top_k
+    assert engine.pair_capacity(8192, 128, 8, 1.25) == 8192 * 10
+    assert engine.pair_capacity(64, 8, 2) == 64 * 4
+    assert engine.pair_capacity(64, 3, 2) == 64 * 3                  # never more than E per token
+    with pytest.raises(ValueError):
+        engine.pair_capacity(64, 8, 2, 0.5)
+
+
+def test_workspace_policy():
+    from usaf_b200 import qwen3moe
+    try:
+        qwen3moe.configure_workspaces(pair_factor=1.25, share_backward=True)
+        assert qwen3moe._POLICY == {"pair_factor": 1.25, "share_backward": True}
+        with pytest.raises(ValueError):
+            qwen3moe.configure_workspaces(pair_factor=0.9)
+    finally:
+        qwen3moe.configure_workspaces()
+    assert qwen3moe._POLICY == {"pair_factor": 2.0, "share_backward": False}
+
+
+def test_model_built_without_dense_experts():
+    """The C3 setup builds its experts without dense tensors (their weights
+    come from the int4 store); everything else is built as usual, and the
+    class is restored afterwards."""
+    from transformers.models.qwen3_moe.configuration_qwen3_moe import Qwen3MoeConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeForCausalLM
+    from usaf_b200 import qwen3moe
+    cfg = Qwen3MoeConfig(vocab_size=64, hidden_size=32, intermediate_size=64, num_hidden_layers=2,
+                         num_attention_heads=4, num_key_value_heads=2, head_dim=8,
+                         moe_intermediate_size=16, num_experts=4, num_experts_per_tok=2,
+                         norm_topk_prob=True)
+    with torch.device("cpu"), qwen3moe.without_dense_experts():
+        lean = Qwen3MoeForCausalLM(cfg)
+    for layer in lean.model.layers:
+        assert layer.mlp.experts.gate_up_proj.numel() == 0
+        assert layer.mlp.experts.down_proj.numel() == 0
+        assert layer.mlp.gate.weight.shape == (4, 32) and layer.mlp.gate.weight.abs().sum() > 0
+        assert not layer.mlp.experts.gate_up_proj.is_meta
+    full = Qwen3MoeForCausalLM(cfg)
+    assert full.model.layers[0].mlp.experts.gate_up_proj.shape == (4, 32, 32)

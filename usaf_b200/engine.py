@@ -16,6 +16,7 @@ overlays, stores).
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 from typing import Optional
 
@@ -259,23 +260,68 @@ class BlockDims:
     dtype: torch.dtype
 
 
+def pair_capacity(T: int, E: int, top_k: int, pair_factor: float = 2) -> int:
+    """Routed (token, expert) pairs a workspace holds: ``T * min(E,
+    ceil(pair_factor * top_k))``.  Threshold ties route a token to more than
+    top_k experts (usaf/qwen3moe_dml.py:79-80), so the default leaves room for
+    twice top_k; a batch with more pairs is refused by the dispatch (error
+    word, :meth:`MoEBlock.check`)."""
+    if pair_factor < 1:
+        raise ValueError("pair_factor must be >= 1 (every token routes to >= top_k experts)")
+    return int(T) * min(int(E), int(math.ceil(pair_factor * top_k)))
+
+
+class BackwardScratch:
+    """Buffers a block uses only inside one call (its backward, and the
+    router's GEMM scratch): the blocks of one model, whose forwards and
+    backwards run one after another on one stream, can share one set.  Sized
+    for ``P_cap`` pairs of T tokens; a block takes leading views."""
+
+    def __init__(self, P_cap: int, T: int, H: int, E: int, I: int, dtype: torch.dtype, device):
+        dev = torch.device(device)
+        f32 = dict(dtype=torch.float32, device=dev)
+        act = dict(dtype=dtype, device=dev)
+        self.key = (int(P_cap), int(T), int(H), int(E), int(I), dtype, dev)
+        self.dcur = torch.empty(P_cap, H, **act)
+        self.dw_pair = torch.empty(P_cap, **f32)
+        self.dgu = torch.empty(P_cap, 2 * I, **act)
+        self.dx_seg = torch.empty(P_cap, H, **act)
+        self.dlogits = torch.empty(T, E, **f32)
+        self.dx_acc = torch.empty(T, H, **f32)
+        self.dx = torch.empty(T, H, **act)
+        self.dw_r = torch.empty(E, H, **act)
+        self.router_ws = torch.empty(max(int(_lib.LIB.usaf_router_workspace_bytes(T, H, E)), 256),
+                                     dtype=torch.uint8, device=dev)
+
+
 class MoEBlock:
     """Workspace + kernel sequence of one MoE block step (single GPU).
 
-    The pair buffers hold ``P_cap = T * min(E, pair_factor * top_k)`` routed
-    (token, expert) pairs; threshold ties can route a token to more than
-    top_k experts, and a batch that overflows the buffer is reported through
-    the device error word (read by :meth:`check`).
+    The pair buffers hold ``P_cap = pair_capacity(T, E, top_k, pair_factor)``
+    routed (token, expert) pairs; threshold ties can route a token to more
+    than top_k experts, and a batch that overflows the buffer is reported
+    through the device error word (read by :meth:`check`).  ``scratch``
+    (a :class:`BackwardScratch` of the same sizes) replaces the block's own
+    backward-only buffers by a set shared with other blocks; the block's
+    results (``dx``, ``dw_r``) then live in that set until the next block's
+    backward, so callers copy them out (the autograd functions do).
     """
 
-    def __init__(self, dims: BlockDims, device, pair_factor: int = 2):
+    def __init__(self, dims: BlockDims, device, pair_factor: float = 2,
+                 scratch: Optional[BackwardScratch] = None):
         self.d = dims
         T, H, E, I = dims.T, dims.H, dims.E, dims.I
         self.device = torch.device(device)
         self.dt = dims.dtype
         self.dtc = _lib.dtype_code(dims.dtype)
-        self.P_cap = T * min(E, pair_factor * dims.top_k)
+        self.P_cap = pair_capacity(T, E, dims.top_k, pair_factor)
         dev, dt, Pc = self.device, self.dt, self.P_cap
+        if scratch is None:
+            scratch = BackwardScratch(Pc, T, H, E, I, dt, dev)
+        elif scratch.key != (Pc, T, H, E, I, dt, dev):
+            raise ValueError(f"shared scratch sized {scratch.key}, block needs "
+                             f"{(Pc, T, H, E, I, dt, dev)}")
+        self.scratch = scratch
         i32 = dict(dtype=torch.int32, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
         act = dict(dtype=dt, device=dev)
@@ -296,21 +342,16 @@ class MoEBlock:
         self.probs = torch.empty(T, E, **f32)
         self.wsum = torch.empty(T, **f32)
         self.weights = torch.empty(T, E, **act)
+        # kept from the forward for the backward
         self.x_perm = torch.empty(Pc, H, **act)
         self.gu = torch.empty(Pc, 2 * I, **act)
         self.h = torch.empty(Pc, I, **act)
         self.y_seg = torch.empty(Pc, H, **act)
         self.y = torch.empty(T, H, **act)
-        self.dcur = torch.empty(Pc, H, **act)
-        self.dw_pair = torch.empty(Pc, **f32)
-        self.dgu = torch.empty(Pc, 2 * I, **act)
-        self.dx_seg = torch.empty(Pc, H, **act)
-        self.dlogits = torch.empty(T, E, **f32)
-        self.dx_acc = torch.empty(T, H, **f32)
-        self.dx = torch.empty(T, H, **act)
-        self.dw_r = torch.empty(E, H, **act)
-        self.router_ws = torch.empty(max(int(_lib.LIB.usaf_router_workspace_bytes(T, H, E)), 256),
-                                     dtype=torch.uint8, device=dev)
+        # used inside one call only (possibly shared between blocks)
+        self.dcur, self.dw_pair, self.dgu = scratch.dcur, scratch.dw_pair, scratch.dgu
+        self.dx_seg, self.dlogits, self.dx_acc = scratch.dx_seg, scratch.dlogits, scratch.dx_acc
+        self.dx, self.dw_r, self.router_ws = scratch.dx, scratch.dw_r, scratch.router_ws
         self.plan = _lib.RoutePlan()
         p = self.plan
         p.T, p.E, p.P_cap = T, E, Pc

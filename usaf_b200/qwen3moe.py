@@ -29,11 +29,12 @@ The router weight receives its gradient through autograd.
 """
 from __future__ import annotations
 
-from typing import Dict, Tuple
+import contextlib
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
-from .engine import BlockDims, MoEBlock, Projection
+from .engine import BackwardScratch, BlockDims, MoEBlock, Projection, pair_capacity
 from .moe_loader import DenseAbsGradStore, SparseGradStore, TopKImportanceStore
 
 
@@ -63,18 +64,60 @@ def _int4_of(experts) -> Tuple[Projection, Projection]:
     return p
 
 
+# Workspace policy of the patched blocks (configure_workspaces)
+_POLICY = {"pair_factor": 2.0, "share_backward": False}
+_SHARED: Dict[tuple, BackwardScratch] = {}
+
+
+def configure_workspaces(pair_factor: float = 2.0, share_backward: bool = False) -> None:
+    """How the patched blocks size their device workspaces (blocks created
+    afterwards; a block keeps its workspace for its lifetime).
+
+    Every block keeps what its backward needs from its forward (permuted
+    tokens, gate/up, h, the routing plan: ~1.1 GB per C3 layer at 8192
+    tokens and ``pair_factor`` 1.25).  ``share_backward`` lets all blocks of
+    the same sizes share one set of their backward-only buffers (the
+    backwards of a model run one after another), which is what makes a deep
+    model fit: ~1 GB once instead of per layer.  ``pair_factor`` sizes the
+    pair buffers at ``T * ceil(pair_factor * top_k)`` pairs: threshold ties
+    add pairs, and a batch that exceeds the buffer is refused (the trainer
+    raises ``UsafError`` on its next host read)."""
+    if pair_factor < 1:
+        raise ValueError("pair_factor must be >= 1")
+    _POLICY["pair_factor"] = float(pair_factor)
+    _POLICY["share_backward"] = bool(share_backward)
+
+
 def _block_for(owner, T: int, H: int, E: int, I: int, top_k: int, norm: bool, dtype, device,
-               pair_factor: int = 2) -> MoEBlock:
+               pair_factor: Optional[float] = None) -> MoEBlock:
     """Workspace of one module for T tokens (kept between the forward and
-    the backward; one per module, so layers do not share it).  It holds
-    T * min(E, pair_factor * top_k) routed pairs."""
+    the backward; one per module, so layers do not share what the backward
+    reads from the forward)."""
+    pf = _POLICY["pair_factor"] if pair_factor is None else pair_factor
     cache: Dict[tuple, MoEBlock] = owner.__dict__.setdefault("_usaf_blocks", {})
-    key = (T, top_k, pair_factor, norm)
+    key = (T, top_k, pf, norm)
     blk = cache.get(key)
     if blk is None:
-        blk = MoEBlock(BlockDims(T, H, E, I, top_k, norm, dtype), device, pair_factor)
+        dims = BlockDims(T, H, E, I, top_k, norm, dtype)
+        scratch = None
+        if _POLICY["share_backward"]:
+            dev = torch.device(device)
+            P_cap = pair_capacity(T, E, top_k, pf)
+            skey = (P_cap, T, H, E, I, dtype, dev)
+            scratch = _SHARED.get(skey)
+            if scratch is None:
+                scratch = _SHARED[skey] = BackwardScratch(P_cap, T, H, E, I, dtype, dev)
+        blk = MoEBlock(dims, device, pf, scratch)
         cache[key] = blk
     return blk
+
+
+def workspaces(model: torch.nn.Module) -> List[MoEBlock]:
+    """Every block workspace the patched forwards created inside ``model``."""
+    out: List[MoEBlock] = []
+    for m in model.modules():
+        out.extend(m.__dict__.get("_usaf_blocks", {}).values())
+    return out
 
 
 def _capture(experts, blk: MoEBlock, gu: Projection, dn: Projection) -> None:
@@ -184,3 +227,29 @@ def patch_qwen3moe_for_b200():
     modeling_qwen3_moe.Qwen3MoeExperts.forward = b200_qwen3_experts_forward
     modeling_qwen3_moe.Qwen3MoeSparseMoeBlock.forward = b200_qwen3_moe_block_forward
     return modeling_qwen3_moe
+
+
+@contextlib.contextmanager
+def without_dense_experts():
+    """Build ``Qwen3MoeExperts`` modules without their dense weight tensors.
+
+    The patched forwards read the int4 store attached with
+    :func:`attach_int4_experts`, never ``gate_up_proj`` / ``down_proj`` (the
+    reference fills those per forward from its cache, train.py:187-197).
+    Inside this context a new experts module gets both as empty parameters
+    on the current default device: a 48-layer C3 model would otherwise
+    allocate 116 GB of fp32 expert weights before they could be quantized."""
+    from transformers.models.qwen3_moe import modeling_qwen3_moe as mq
+    orig = mq.Qwen3MoeExperts.__init__
+
+    def init(self, config):
+        with torch.device("meta"):
+            orig(self, config)
+        self.gate_up_proj = torch.nn.Parameter(torch.empty(0), requires_grad=False)
+        self.down_proj = torch.nn.Parameter(torch.empty(0), requires_grad=False)
+
+    mq.Qwen3MoeExperts.__init__ = init
+    try:
+        yield
+    finally:
+        mq.Qwen3MoeExperts.__init__ = orig

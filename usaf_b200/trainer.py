@@ -25,7 +25,9 @@ weights from :func:`usaf_b200.qwen3moe.attach_int4_experts`):
   same weight decay over the gate weights of the blocks whose experts train.
 
 Everything stays on the device; one host read per step carries the
-finiteness flag and the loss.
+finiteness flag, the loss and the error words of the block workspaces (a
+batch whose routed pairs exceed a workspace raises ``UsafError`` there,
+before any update).
 """
 from __future__ import annotations
 
@@ -35,7 +37,8 @@ from typing import Any, Callable, Dict, Iterable, List, Optional
 import torch
 
 from . import checkpoint as ckpt
-from . import rigl
+from . import qwen3moe, rigl
+from ._lib import UsafError
 from .engine import Projection
 from .moe_loader import SparseGradStore, TopKImportanceStore
 from .sparse_optim import SparseAdam
@@ -224,8 +227,17 @@ class SparseTrainer:
         denom = scale * self.accum
         # train.py:662-663: the step runs only if every expert gradient is finite
         flags = torch.stack([torch.isfinite(g).all() for g in self.store.compact.values()])
-        host = torch.cat([flags.float(), loss_sum.reshape(1)]).cpu()
-        finite = bool(host[:-1].all())
+        blocks = qwen3moe.workspaces(self.model)
+        nf = flags.numel()
+        host = torch.cat([flags.float(), loss_sum.reshape(1)] +
+                         [b.err.float() for b in blocks]).cpu()
+        if bool(host[nf + 1:].any()):
+            for b in blocks:
+                b.err.zero_()
+            self.step_num -= 1
+            raise UsafError("a block workspace reported a device error in this step (routed "
+                            "pairs beyond its buffer, or a timed-out wait); no update applied")
+        finite = bool(host[:nf].all())
         if finite:
             self.opt.step(compact_grads=self.store.compact, grad_div=denom)
             if self.router_opt is not None:
@@ -237,7 +249,7 @@ class SparseTrainer:
         elif self.router_opt is not None:
             self.router_opt.zero_grad()
         self.scaler.update(finite)
-        loss = float(host[-1]) / self.accum
+        loss = float(host[nf]) / self.accum
         self.losses.append(loss)
         return {"step": step, "loss": loss, "lr": lr, "scale": self.scaler.scale,
                 "finite": finite}
