@@ -1,0 +1,86 @@
+"""The autograd glue of the patched Qwen3-MoE block (no GPU): the block
+workspace keeps the forward's state for the backward, so a model whose decoder
+layers recompute their activations in the backward (non-reentrant checkpointing,
+as the full-depth setup uses) must produce the same gradients as one that
+keeps them.  The device block is replaced by a CPU stand-in with the same
+call pattern and the same kind of state (its backward reads what its last
+forward stored, not what autograd saved)."""
+import torch
+
+from usaf_b200 import qwen3moe
+
+
+class _StandInBlock:
+    """forward: y = tanh(hs W_r^T) P, state kept on the object; backward reads it."""
+
+    def __init__(self, E, H, seed):
+        g = torch.Generator().manual_seed(seed)
+        self.P = torch.randn(E, H, generator=g) * 0.1
+        self.state = None
+        self.forwards = 0
+
+    def forward(self, hs, w_r, gu, dn):
+        self.forwards += 1
+        self.state = torch.tanh(hs.float() @ w_r.float().t())
+        return (self.state @ self.P).to(hs.dtype)
+
+    def backward(self, dy, hs, w_r, gu, dn):
+        t = self.state                                     # the last forward's state
+        dl = (dy.float() @ self.P.t()) * (1 - t * t)
+        return (dl @ w_r.float()).to(hs.dtype), (dl.t() @ hs.float()).to(w_r.dtype)
+
+
+class _Dn:
+    C = 16
+
+
+def _grads(recompute: bool, monkeypatch):
+    from transformers.models.qwen3_moe.configuration_qwen3_moe import Qwen3MoeConfig
+    from transformers.models.qwen3_moe.modeling_qwen3_moe import Qwen3MoeForCausalLM
+    blocks = {}
+
+    def block_for(owner, T, H, E, I, top_k, norm, dtype, device, pair_factor=None):
+        key = id(owner)
+        if key not in blocks:
+            blocks[key] = _StandInBlock(E, H, seed=len(blocks))
+        return blocks[key]
+
+    monkeypatch.setattr(qwen3moe, "_block_for", block_for)
+    monkeypatch.setattr(qwen3moe, "_int4_of", lambda experts: (None, _Dn()))
+    cfg = Qwen3MoeConfig(vocab_size=64, hidden_size=32, intermediate_size=64, num_hidden_layers=3,
+                         num_attention_heads=4, num_key_value_heads=2, head_dim=8,
+                         moe_intermediate_size=16, num_experts=4, num_experts_per_tok=2,
+                         norm_topk_prob=True, attention_dropout=0.0)
+    torch.manual_seed(0)
+    with torch.device("cpu"), qwen3moe.without_dense_experts():
+        model = Qwen3MoeForCausalLM(cfg)
+    for p in model.parameters():
+        p.requires_grad_(False)
+    gates = [layer.mlp.gate.weight for layer in model.model.layers]
+    for w in gates:
+        w.requires_grad_(True)
+    if recompute:
+        model.gradient_checkpointing_enable(gradient_checkpointing_kwargs={"use_reentrant": False})
+    model.train()
+    ids = torch.randint(0, 64, (2, 12), generator=torch.Generator().manual_seed(1))
+    loss = model(input_ids=ids, labels=ids).loss
+    loss.backward()
+    return loss.detach(), [w.grad.clone() for w in gates], sum(b.forwards for b in blocks.values())
+
+
+def test_recompute_gives_the_same_gradients(monkeypatch):
+    from transformers.models.qwen3_moe import modeling_qwen3_moe as mq
+    orig = (mq.Qwen3MoeSparseMoeBlock.forward, mq.Qwen3MoeExperts.forward)
+    qwen3moe.patch_qwen3moe_for_b200()
+    try:
+        with monkeypatch.context() as m:
+            loss_a, grads_a, fwd_a = _grads(False, m)
+        with monkeypatch.context() as m:
+            loss_b, grads_b, fwd_b = _grads(True, m)
+    finally:
+        mq.Qwen3MoeSparseMoeBlock.forward, mq.Qwen3MoeExperts.forward = orig
+    assert fwd_a == 3 and fwd_b == 6          # recompute ran every block's forward again
+    assert torch.equal(loss_a, loss_b)
+    for a, b in zip(grads_a, grads_b):
+        assert a.abs().sum() > 0
+        assert torch.equal(a, b)
