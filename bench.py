@@ -460,6 +460,7 @@ def run_c4_sweep(steps: int = 10):
         p.set_overlay(idx, torch.randn(idx.numel(), device=dev, generator=g) * 0.02)
         projs[n] = p
     gu, dn = projs["gate_up_proj"], projs["down_proj"]
+    hbm_peak, tc_peak, _ = peaks()
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     for routing in ("uniform", "zipf1.2"):
         for T in (1, 16, 256, 4096, 16384):
@@ -494,10 +495,19 @@ def run_c4_sweep(steps: int = 10):
             blk.check()
             P = blk.n_pairs_host()
             fwd_flop = 2.0 * P * 3 * I * H
+            # HBM floor of the grouped GEMMs: the int4 codes + fp16 scale/zero of every
+            # expert hit, read once per pass (gate_up + down forward; down_bwd + gate_up_bwd)
+            hit = int((blk.expert_cnt > 0).sum().item())
+            w_bytes = hit * 3 * I * H * (0.5 + 4.0 / 128)
+            fwd_s, bwd_s = tf / steps * 1e-3, tb / steps * 1e-3
             print(json.dumps({"config": "C4", "routing": routing, "T": T, "pairs": P,
                               "fwd_ms": tf / steps, "bwd_ms": tb / steps,
-                              "fwd_tflops": fwd_flop / (tf / steps * 1e-3) / 1e12,
-                              "bwd_tflops": fwd_flop / (tb / steps * 1e-3) / 1e12,
+                              "fwd_tflops": fwd_flop / fwd_s / 1e12,
+                              "bwd_tflops": fwd_flop / bwd_s / 1e12,
+                              "experts_hit": hit, "weight_mb_per_pass": w_bytes / 1e6,
+                              "fwd_weight_gbps": w_bytes / fwd_s / 1e9,
+                              "fwd_hbm_frac": w_bytes / fwd_s / 1e9 / hbm_peak,
+                              "fwd_tensor_frac": fwd_flop / fwd_s / 1e12 / tc_peak,
                               "max_expert_tokens": int(blk.expert_cnt.max().item())}), flush=True)
             del blk
 
