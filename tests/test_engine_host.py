@@ -116,3 +116,16 @@ def test_model_built_without_dense_experts():
         assert not layer.mlp.experts.gate_up_proj.is_meta
     full = Qwen3MoeForCausalLM(cfg)
     assert full.model.layers[0].mlp.experts.gate_up_proj.shape == (4, 32, 32)
+
+
+def test_shared_scratch_must_match_the_block():
+    dims = engine.BlockDims(T=8, H=256, E=4, I=128, top_k=2, norm_topk_prob=True,
+                            dtype=torch.bfloat16)
+    P_cap = engine.pair_capacity(8, 4, 2, 2)
+    wrong = engine.BackwardScratch(P_cap + 1, 8, 256, 4, 128, torch.bfloat16, "cpu")
+    with pytest.raises(ValueError):
+        engine.MoEBlock(dims, "cpu", 2, wrong)
+    right = engine.BackwardScratch(P_cap, 8, 256, 4, 128, torch.bfloat16, "cpu")
+    assert right.dcur.shape == (P_cap, 256) and right.dgu.shape == (P_cap, 256)
+    with pytest.raises(TypeError):        # sizes agree; CPU tensors never reach a kernel
+        engine.MoEBlock(dims, "cpu", 2, right)
