@@ -129,3 +129,14 @@ def test_shared_scratch_must_match_the_block():
     assert right.dcur.shape == (P_cap, 256) and right.dgu.shape == (P_cap, 256)
     with pytest.raises(TypeError):        # sizes agree; CPU tensors never reach a kernel
         engine.MoEBlock(dims, "cpu", 2, right)
+
+
+def test_rigl_merge_with_an_empty_active_set():
+    """The grown budget is len(old) - len(kept): an empty old set stays empty
+    (and never reaches the device search)."""
+    from usaf_b200 import rigl
+    empty = torch.empty(0, dtype=torch.long)
+    fin, vals = rigl.merge(empty, torch.tensor([3, 1, 2]), torch.empty(0), torch.zeros(8))
+    assert fin.numel() == 0 and vals.numel() == 0
+    fin, vals = rigl.merge(torch.tensor([4, 2]), None, torch.tensor([0.5, 0.25]), torch.zeros(8))
+    assert fin.tolist() == [4, 2] and vals.tolist() == [0.5, 0.25]

@@ -19,9 +19,10 @@ from . import engine
 def merge(old: torch.Tensor, new: Optional[torch.Tensor], old_masters: torch.Tensor,
           original_flat: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     dev = old.device
-    if new is None or new.numel() == 0:
-        return old.clone(), old_masters.clone()
     n_old = old.numel()
+    if new is None or new.numel() == 0 or n_old == 0:
+        # nothing new, or nothing to replace: the budget is len(old) (train.py:563-565)
+        return old.clone(), old_masters.clone()
     old_s, old_pos = engine.sort_u32(old, torch.arange(n_old, device=dev))
     new_s, _ = engine.sort_u32(new.to(dev), torch.arange(new.numel(), device=dev))
     old_s = old_s.long()
