@@ -140,3 +140,12 @@ def test_rigl_merge_with_an_empty_active_set():
     assert fin.numel() == 0 and vals.numel() == 0
     fin, vals = rigl.merge(torch.tensor([4, 2]), None, torch.tensor([0.5, 0.25]), torch.zeros(8))
     assert fin.tolist() == [4, 2] and vals.tolist() == [0.5, 0.25]
+
+
+def test_csr_order_refuses_out_of_range_indices():
+    q, s, z = _q4(2, 16, 256)
+    p = Projection(q, s, z, (2, 16, 256), 128, torch.float32)
+    with pytest.raises(IndexError):
+        p.csr_order(torch.tensor([5, p.numel()]))
+    with pytest.raises(IndexError):
+        p.csr_order(torch.tensor([-3]))

@@ -103,7 +103,11 @@ def export_merged_weights(quant_path: str, masters: Dict[str, torch.Tensor],
             continue
         if fname in masters and fname in active_idx:
             aidx = active_idx[fname].reshape(-1).to(device=dev, dtype=torch.long)
-            trained = masters[fname].detach().to(device=dev, dtype=torch.float16)
+            trained = masters[fname].detach().to(device=dev, dtype=torch.float16).reshape(-1)
+            if aidx.numel() != trained.numel():
+                raise ValueError(f"{fname}: {trained.numel()} masters for {aidx.numel()} indices")
+            if aidx.numel() and (int(aidx.min()) < 0 or int(aidx.max()) >= t.numel()):
+                raise IndexError(f"{fname}: active index out of range")
             flat = t.reshape(-1).clone()
             flat.scatter_(0, aidx, trained)
             t = flat.reshape(t.shape)

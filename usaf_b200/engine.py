@@ -164,6 +164,9 @@ class Projection:
         in this order makes every compact <-> CSR map the identity, so the
         gradient scatter and the optimizer's overlay write-back stream."""
         idx = idx.reshape(-1).to(device=self.device, dtype=torch.int64)
+        if idx.numel() and (int(idx.min()) < 0 or int(idx.max()) >= self.numel()):
+            # callers index the dequantized tensor with these next; refuse them here
+            raise IndexError(f"active index out of range [0, {self.numel()})")
         E, R, Cc = self.E, self.R, self.C
         e = idx // (R * Cc)
         r = (idx // Cc) % R
