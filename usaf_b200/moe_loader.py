@@ -59,10 +59,12 @@ class SparseGradStore:
             return
         if not g.is_cuda:
             raise TypeError("usaf_b200 stores take CUDA gradients")
+        slice_size = _numel(self.shapes[full_name][1:])
+        if g.numel() != slice_size:
+            raise ValueError(f"{full_name}: expert gradient of {g.numel()} elements, expected {slice_size}")
         key = (full_name, int(ei))
         if key not in self._local:
             idx = self.active_idx[full_name]
-            slice_size = _numel(self.shapes[full_name][1:])
             pos = ((idx // slice_size) == ei).nonzero().reshape(-1)
             self._local[key] = (idx[pos] - ei * slice_size, pos)
         local, pos = self._local[key]
