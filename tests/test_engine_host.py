@@ -149,3 +149,18 @@ def test_csr_order_refuses_out_of_range_indices():
         p.csr_order(torch.tensor([5, p.numel()]))
     with pytest.raises(IndexError):
         p.csr_order(torch.tensor([-3]))
+
+
+def test_dequantize_checks_the_layout_sizes():
+    from usaf_b200.quantization import dequantize_4bit
+    q, s, z = _q4(1, 4, 256)                        # 1024 elements: 8 groups of 128
+    with pytest.raises(ValueError):
+        dequantize_4bit(q[:-1], s, z, (4, 256))
+    with pytest.raises(ValueError):
+        dequantize_4bit(q, s[:-1], z, (4, 256))
+    with pytest.raises(ValueError):
+        dequantize_4bit(q, s, z.float(), (4, 256))
+    with pytest.raises(ValueError):
+        dequantize_4bit(q, s, z, (8, 256))          # shape larger than the codes
+    with pytest.raises(TypeError):                  # consistent sizes, CPU tensors: no fallback
+        dequantize_4bit(q, s, z, (4, 256))

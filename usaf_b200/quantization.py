@@ -44,6 +44,15 @@ def quantize_4bit(tensor: torch.Tensor, group_size: int = 128
 def dequantize_4bit(q_int4: torch.Tensor, scale: torch.Tensor, zero: torch.Tensor, shape,
                     group_size: int = 128, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
     numel = _numel(shape)
+    # sizes of the quantize_4bit layout for this shape: the kernel reads exactly these
+    egs = min(group_size, numel) if numel else group_size
+    ng = (numel + egs - 1) // egs if numel else 0
+    if q_int4.numel() != ng * ((egs + 1) // 2) or q_int4.dtype not in (torch.int8, torch.uint8):
+        raise ValueError(f"q: expected {ng * ((egs + 1) // 2)} int8 bytes for shape {tuple(shape)} "
+                         f"(group {group_size}), got {q_int4.numel()} {q_int4.dtype}")
+    for nm, t in (("scale", scale), ("zero", zero)):
+        if t.numel() != ng or t.dtype != torch.float16:
+            raise ValueError(f"{nm}: expected {ng} fp16 values, got {t.numel()} {t.dtype}")
     out = torch.empty(numel, dtype=out_dtype, device=q_int4.device)
     # keep the contiguous copies alive until the kernel is enqueued
     q, s, z = q_int4.contiguous(), scale.contiguous(), zero.contiguous()
