@@ -98,6 +98,9 @@ class TopKImportanceStore:
         if not g.is_cuda:
             raise TypeError("usaf_b200 stores take CUDA gradients")
         flat = g.detach().float().reshape(-1).abs()
+        if flat.numel() != _numel(self._shapes[full_name][1:]):
+            raise ValueError(f"{full_name}: expert gradient of {flat.numel()} elements, expected "
+                             f"{_numel(self._shapes[full_name][1:])}")
         k = min(self._k_of(flat.numel()), flat.numel())
         v, i = engine.topk_desc(flat, k, idx_base=int(ei) * flat.numel())
         self._vals[full_name][int(ei)] = v
@@ -113,6 +116,9 @@ class TopKImportanceStore:
             return
         E = absg.shape[0]
         numel_e = absg[0].numel()
+        if numel_e != _numel(self._shapes[full_name][1:]):
+            raise ValueError(f"{full_name}: |grad| slices of {numel_e} elements, expected "
+                             f"{_numel(self._shapes[full_name][1:])}")
         k = min(self._k_of(numel_e), numel_e)
         hit = range(E) if experts is None else experts.tolist()
         for ei in hit:
