@@ -84,3 +84,38 @@ def test_recompute_gives_the_same_gradients(monkeypatch):
     for a, b in zip(grads_a, grads_b):
         assert a.abs().sum() > 0
         assert torch.equal(a, b)
+
+
+def test_blocks_share_backward_scratch_when_configured(monkeypatch):
+    """With share_backward, every block of the same sizes gets the same
+    backward-only buffers and its own forward state; without it, each block
+    allocates its own set."""
+    made = []
+
+    class _Scratch:
+        def __init__(self, *a):
+            self.args = a
+
+    class _Block:
+        def __init__(self, dims, device, pair_factor, scratch=None):
+            self.scratch, self.pf = scratch, pair_factor
+            made.append(self)
+
+    monkeypatch.setattr(qwen3moe, "BackwardScratch", _Scratch)
+    monkeypatch.setattr(qwen3moe, "MoEBlock", _Block)
+    monkeypatch.setattr(qwen3moe, "_SHARED", {})
+    owners = [torch.nn.Module() for _ in range(3)]
+    try:
+        qwen3moe.configure_workspaces(pair_factor=1.25, share_backward=True)
+        blks = [qwen3moe._block_for(o, 64, 32, 4, 16, 2, True, torch.bfloat16, "cpu") for o in owners]
+        assert len({id(b) for b in blks}) == 3                      # forward state per layer
+        assert len({id(b.scratch) for b in blks}) == 1              # one backward set
+        assert blks[0].scratch.args[0] == 64 * 3 and blks[0].pf == 1.25   # ceil(1.25 * 2) pairs/token
+        assert qwen3moe._block_for(owners[0], 64, 32, 4, 16, 2, True, torch.bfloat16, "cpu") is blks[0]
+        assert qwen3moe.workspaces(torch.nn.ModuleList(owners)) == blks
+        qwen3moe.configure_workspaces()
+        other = torch.nn.Module()
+        b = qwen3moe._block_for(other, 64, 32, 4, 16, 2, True, torch.bfloat16, "cpu")
+        assert b.scratch is None and b.pf == 2.0                    # the block allocates its own
+    finally:
+        qwen3moe.configure_workspaces()
