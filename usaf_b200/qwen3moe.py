@@ -50,11 +50,23 @@ def int4_projection(entry, shape, group_size: int = 128, dtype=torch.bfloat16,
     return Projection(q.to(dev), s.to(dev), z.to(dev), shape, group_size, dtype)
 
 
-def attach_int4_experts(experts: torch.nn.Module, gate_up: Projection, down: Projection) -> None:
-    """Give a ``Qwen3MoeExperts`` module its int4 expert weights."""
+def attach_int4_experts(experts: torch.nn.Module, gate_up: Projection, down: Projection,
+                        expert_parallel: bool = False, group=None) -> None:
+    """Give a ``Qwen3MoeExperts`` module its int4 expert weights.
+
+    ``expert_parallel``: the experts are sharded over the torch.distributed
+    ``group`` (None: the default group); this rank's ``gate_up`` / ``down``
+    hold its E/W experts ([E/W, 2I, H] and [E/W, H, I]) and rank r owns
+    experts [r E/W, (r+1) E/W).  Every rank routes its own tokens with the
+    replicated router; the block exchanges rows with the experts' owners over
+    NCCL, and the router gradient is summed over the ranks.  Captured
+    gradients are those of this rank's experts under the full tensors'
+    names and flat indices."""
     if gate_up.E != down.E or gate_up.C != down.R or gate_up.R != 2 * down.C:
         raise ValueError("gate_up [E,2I,H] and down [E,H,I] shapes do not match")
     experts._usaf_int4 = (gate_up, down)
+    experts._usaf_ep = bool(expert_parallel)
+    experts._usaf_ep_group = group
 
 
 def _int4_of(experts) -> Tuple[Projection, Projection]:
@@ -112,11 +124,26 @@ def _block_for(owner, T: int, H: int, E: int, I: int, top_k: int, norm: bool, dt
     return blk
 
 
+def _ep_for(owner, T: int, w_r: torch.Tensor, top_k: int, norm: bool, gu: Projection,
+            dn: Projection, group):
+    """Expert-parallel workspace of one module for T tokens (one per module)."""
+    from .expert_parallel import ExpertParallelMoE
+    cache = owner.__dict__.setdefault("_usaf_ep_moes", {})
+    key = (T, top_k, norm)
+    moe = cache.get(key)
+    if moe is None:
+        moe = ExpertParallelMoE(w_r, gu, dn, top_k, T, norm, group, _POLICY["pair_factor"])
+        cache[key] = moe
+    return moe
+
+
 def workspaces(model: torch.nn.Module) -> List[MoEBlock]:
-    """Every block workspace the patched forwards created inside ``model``."""
+    """Every block workspace the patched forwards created inside ``model``
+    (the source-side block of each expert-parallel workspace included)."""
     out: List[MoEBlock] = []
     for m in model.modules():
         out.extend(m.__dict__.get("_usaf_blocks", {}).values())
+        out.extend(ep.src for ep in m.__dict__.get("_usaf_ep_moes", {}).values())
     return out
 
 
@@ -177,6 +204,63 @@ class _BlockFn(torch.autograd.Function):
         return dx.clone(), (dw_r.clone() if ctx.needs_input_grad[1] else None), None
 
 
+class _EPBlockFn(torch.autograd.Function):
+    """Router + experts of one block with the experts sharded over ranks
+    (``attach_int4_experts(..., expert_parallel=True)``)."""
+
+    @staticmethod
+    def forward(ctx, hs, w_r, block):
+        experts = block.experts
+        gu, dn = _int4_of(experts)
+        moe = _ep_for(block, hs.shape[0], w_r, block.gate.top_k, bool(block.gate.norm_topk_prob),
+                      gu, dn, experts._usaf_ep_group)
+        y = moe.forward(hs, w_r).clone()
+        ctx.block, ctx.moe = block, moe
+        ctx.save_for_backward(hs, w_r)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        hs, w_r = ctx.saved_tensors
+        moe, experts = ctx.moe, ctx.block.experts
+        cap = getattr(experts, "_grad_capture", None)
+        cg = cd = None
+        if cap is not None and isinstance(cap[0], SparseGradStore):
+            store, prefix = cap
+            gu, dn = _int4_of(experts)
+            cg = store.compact.get(f"{prefix}.gate_up_proj")
+            cd = store.compact.get(f"{prefix}.down_proj")
+            for c, p, nm in ((cg, gu, "gate_up_proj"), (cd, dn, "down_proj")):
+                if c is not None and p.n_ov != c.numel():
+                    raise ValueError(f"{prefix}.{nm}: overlay and store hold different active sets")
+            if cg is None or cd is None:   # one vector missing: a zero-length stand-in
+                cg = cg if cg is not None else torch.zeros(gu.n_ov, device=hs.device)
+                cd = cd if cd is not None else torch.zeros(dn.n_ov, device=hs.device)
+        dx, dw_r = moe.backward(dy.contiguous(), hs, w_r, reduce_router=True, compact_gu=cg,
+                                compact_dn=cd)
+        if cap is not None and not isinstance(cap[0], SparseGradStore):
+            _capture_ep(experts, moe, cap)
+        return dx.clone(), (dw_r.clone() if ctx.needs_input_grad[1] else None), None
+
+
+def _capture_ep(experts, moe, cap) -> None:
+    """Importance captures of this rank's experts, numbered as experts of the
+    full tensors (``expert_offset``); the per-tensor selection over all ranks
+    is the caller's (``expert_parallel.global_select``)."""
+    store, prefix = cap
+    e0 = moe.rank * moe.El
+    if isinstance(store, TopKImportanceStore):
+        hit = (moe.own_cnt > 0).nonzero().reshape(-1)
+        for which in ("gate_up_proj", "down_proj"):
+            store.add_dense_abs(f"{prefix}.{which}", moe.dense_abs_grad(which), hit, expert_offset=e0)
+    elif isinstance(store, DenseAbsGradStore):
+        for which in ("gate_up_proj", "down_proj"):
+            store.add_dense_abs(f"{prefix}.{which}", moe.dense_abs_grad(which), expert_offset=e0)
+    else:
+        raise TypeError("usaf_b200 captures into SparseGradStore / TopKImportanceStore / "
+                        f"DenseAbsGradStore, not {type(store).__name__}")
+
+
 class _ExpertsFn(torch.autograd.Function):
     """Experts with caller-given dense weights (the reference's
     ``experts(hidden_states, weights)`` call)."""
@@ -206,7 +290,8 @@ def b200_qwen3_moe_block_forward(self, hidden_states: torch.Tensor) -> torch.Ten
     """``dml_qwen3_moe_block_forward`` (usaf/qwen3moe_dml.py:67-86) on B200."""
     batch_size, sequence_length, hidden_dim = hidden_states.shape
     hs = hidden_states.reshape(-1, hidden_dim).contiguous()
-    y = _BlockFn.apply(hs, self.gate.weight, self)
+    fn = _EPBlockFn if getattr(self.experts, "_usaf_ep", False) else _BlockFn
+    y = fn.apply(hs, self.gate.weight, self)
     return y.view(batch_size, sequence_length, hidden_dim)
 
 
@@ -217,6 +302,9 @@ def b200_qwen3_experts_forward(self, hidden_states: torch.Tensor, weights: torch
     ``dy[t] . y_e[t]`` at routed entries and 0 elsewhere; the reference's
     dense-masked loop also fills the off-route entries, which its block
     discards through the routing mask."""
+    if getattr(self, "_usaf_ep", False):
+        raise NotImplementedError("expert-parallel experts run through the block forward "
+                                  "(Qwen3MoeSparseMoeBlock), which routes and exchanges the tokens")
     return _ExpertsFn.apply(hidden_states.contiguous(), weights, self)
 
 
