@@ -22,7 +22,13 @@ weights from :func:`usaf_b200.qwen3moe.attach_int4_experts`):
   importance pass on the step's first micro-batch, the kept/grown merge of
   :func:`usaf_b200.rigl.merge`, fresh SparseAdam state;
 * router optimizer (train.py:494-498, 667-672): SGD with momentum 0.9 and the
-  same weight decay over the gate weights of the blocks whose experts train.
+  same weight decay over the gate weights of the blocks whose experts train;
+* experts sharded over ranks (``attach_int4_experts(..., expert_parallel=True)``):
+  every rank trains its shard's coordinates, the importance selection is the
+  per-tensor top-k over all ranks' candidates (the single-process selection
+  over the union of the ranks' batches), the router gradient is summed over
+  the ranks, and every rank takes the same skip / raise decision; each rank
+  saves its own checkpoint file.
 
 Everything stays on the device; one host read per step carries the
 finiteness flag, the loss and the error words of the block workspaces (a
@@ -35,11 +41,13 @@ import math
 from typing import Any, Callable, Dict, Iterable, List, Optional
 
 import torch
+import torch.distributed as dist
 
 from . import checkpoint as ckpt
 from . import qwen3moe, rigl
 from ._lib import UsafError
 from .engine import Projection
+from .expert_parallel import global_select
 from .moe_loader import SparseGradStore, TopKImportanceStore
 from .sparse_optim import SparseAdam
 
@@ -113,6 +121,18 @@ class SparseTrainer:
             self.projections[f"{n}.gate_up_proj"] = gu
             self.projections[f"{n}.down_proj"] = dn
         self.shapes = {n: p.shape for n, p in self.projections.items()}
+        # experts sharded over ranks (attach_int4_experts(..., expert_parallel=True)):
+        # the projections are this rank's shards; selection runs over the full tensors
+        ep = {bool(getattr(m, "_usaf_ep", False)) for m in self.experts.values()}
+        if len(ep) > 1:
+            raise ValueError("either every expert module is sharded over ranks or none is")
+        self.expert_parallel = ep == {True}
+        self.ep_group = (next(iter(self.experts.values()))._usaf_ep_group
+                         if self.expert_parallel else None)
+        if self.expert_parallel:
+            W = dist.get_world_size(self.ep_group)
+            self.ep_rank = dist.get_rank(self.ep_group)
+            self.full_shapes = {n: (sh[0] * W,) + tuple(sh[1:]) for n, sh in self.shapes.items()}
         self.router_params: Dict[str, torch.nn.Parameter] = {}
         if train_router:
             for n in self.experts:
@@ -143,7 +163,8 @@ class SparseTrainer:
     def importance(self, batch, loss_fn: LossFn) -> Dict[str, torch.Tensor]:
         """Dense importance pass (train.py:386-402, 540-546): the top ``frac`` of
         |dW| per tensor on one micro-batch."""
-        store = TopKImportanceStore(self.shapes, frac=self.frac)
+        store = TopKImportanceStore(self.full_shapes if self.expert_parallel else self.shapes,
+                                    frac=self.frac)
         self._set_capture(store)
         try:
             self._backward(loss_fn, batch)
@@ -151,7 +172,20 @@ class SparseTrainer:
             self._set_capture(self.store) if self.store is not None else self._clear_capture()
         for p in self.router_params.values():
             p.grad = None
-        return store.select(self.frac)
+        if not self.expert_parallel:
+            return store.select(self.frac)
+        # per full tensor: top-k over every rank's candidates, then this rank's share
+        # as flat indices of its shard
+        dev = next(iter(self.projections.values())).device
+        out: Dict[str, torch.Tensor] = {}
+        for name, shape in self.full_shapes.items():
+            vals, idxs = store.candidate_list(name, device=dev)
+            k = max(1, int(math.prod(shape) * self.frac))
+            g = global_select(vals, idxs, k, self.ep_group)
+            span = math.prod(self.shapes[name])
+            lo = self.ep_rank * span
+            out[name] = g[(g >= lo) & (g < lo + span)] - lo
+        return out
 
     def _clear_capture(self) -> None:
         for m in self.experts.values():
@@ -229,8 +263,16 @@ class SparseTrainer:
         flags = torch.stack([torch.isfinite(g).all() for g in self.store.compact.values()])
         blocks = qwen3moe.workspaces(self.model)
         nf = flags.numel()
-        host = torch.cat([flags.float(), loss_sum.reshape(1)] +
-                         [b.err.float() for b in blocks]).cpu()
+        dev_vals = torch.cat([flags.float(), loss_sum.reshape(1)] + [b.err.float() for b in blocks])
+        if self.expert_parallel:
+            # every rank takes the same decision: skip if any shard is non-finite, raise if
+            # any rank's workspace flagged an error; the logged loss is the ranks' mean
+            agg = torch.cat([(1.0 - dev_vals[:nf]), dev_vals[nf:nf + 1],
+                             (dev_vals[nf + 1:] != 0).float().sum().reshape(1)])
+            dist.all_reduce(agg, group=self.ep_group)
+            W = dist.get_world_size(self.ep_group)
+            dev_vals = torch.cat([(agg[:nf] == 0).float(), agg[nf:nf + 1] / W, agg[nf + 1:]])
+        host = dev_vals.cpu()
         if bool(host[nf + 1:].any()):
             for b in blocks:
                 b.err.zero_()
