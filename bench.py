@@ -566,7 +566,8 @@ def run_c5(steps: int = 10, warmup: int = 3):
 
 
 def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2, recompute: bool = True):
-    """BASELINE configs[2] (C3) on one GPU: a random-init Qwen3MoeForCausalLM
+    """BASELINE configs[2] (C3), on one GPU or, under torchrun, with the experts
+    sharded over the ranks (each rank its own micro-batch): a random-init Qwen3MoeForCausalLM
     with the C3 shapes (H 2048, 32/4 heads, head dim 128, E 128, top-8, I 768,
     vocab 151936) at ``n_layers`` of its 48 layers, int4 g128 experts attached
     through patch_qwen3moe_for_b200, sequence 2048 x micro-batch 4, LM
@@ -584,11 +585,17 @@ def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2, recompute: bool =
     from usaf_b200.engine import Projection
     from usaf_b200.quantization import quantize_4bit
     from usaf_b200.trainer import SparseTrainer
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
+    if world > 1:   # experts sharded over the ranks, every rank its own micro-batch
+        torch.distributed.init_process_group(
+            "nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
     qwen3moe.patch_qwen3moe_for_b200()
     qwen3moe.configure_workspaces(pair_factor=1.25, share_backward=True)
     H, E, k, I, V, S, MB = 2048, 128, 8, 768, 151936, 2048, 4
+    El, e0 = E // world, rank * (E // world)
     cfg = Qwen3MoeConfig(vocab_size=V, hidden_size=H, intermediate_size=6144, num_hidden_layers=n_layers,
                          num_attention_heads=32, num_key_value_heads=4, head_dim=128,
                          moe_intermediate_size=I, num_experts=E, num_experts_per_tok=k,
@@ -607,12 +614,19 @@ def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2, recompute: bool =
         mlp.gate.weight.requires_grad_(True)
         ps = []
         for shape in ((E, 2 * I, H), (E, H, I)):
-            w = torch.randn(*shape, device=dev, generator=g) * 0.02
-            q, s_, z, _ = quantize_4bit(w, 128)
-            del w
-            ps.append(Projection(q, s_, z, shape, 128, torch.bfloat16))
-        qwen3moe.attach_int4_experts(mlp.experts, *ps)
-    gt = torch.Generator(device=dev).manual_seed(4)
+            # the same full tensor on every rank (one generator stream); this rank keeps its shard
+            rows = []
+            for e in range(E):
+                w_e = torch.randn(*shape[1:], device=dev, generator=g) * 0.02
+                if e0 <= e < e0 + El:
+                    rows.append(w_e)
+            shard = torch.stack(rows)
+            del rows
+            q, s_, z, _ = quantize_4bit(shard, 128)
+            del shard
+            ps.append(Projection(q, s_, z, (El,) + shape[1:], 128, torch.bfloat16))
+        qwen3moe.attach_int4_experts(mlp.experts, *ps, expert_parallel=world > 1)
+    gt = torch.Generator(device=dev).manual_seed(4 + rank)
     batches = [torch.randint(0, V, (MB, S), device=dev, generator=gt) for _ in range(2)]
     lm = lambda m, ids: m(input_ids=ids, labels=ids).loss  # noqa: E731
     tr = SparseTrainer(model, steps=1000, lr_peak=2e-4, accum=1, frac=0.005, reselect_every=10 ** 9)
@@ -626,10 +640,20 @@ def run_c3(n_layers: int = 2, steps: int = 5, warmup: int = 2, recompute: bool =
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / steps
+    if world > 1:   # the slowest rank's time (CUDA events), whole-job tokens
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
     print(json.dumps({"config": "C3", "workload": f"Qwen3-30B-A3B-shaped causal LM, {n_layers} of 48 layers "
-                      "(C3 layer shapes), seq 2048 x mb 4, LM cross-entropy, int4 experts, 0.5% sparse, "
-                      "SparseTrainer steps", "layers": n_layers, "tokens_per_step": MB * S,
-                      "step_ms": ms, "tokens_per_s": MB * S / (ms * 1e-3),
+                      "(C3 layer shapes), seq 2048 x mb 4 per GPU, LM cross-entropy, int4 experts, 0.5% "
+                      "sparse, SparseTrainer steps", "layers": n_layers, "n_gpus": world,
+                      "parallelism": f"ep{world}" if world > 1 else "single",
+                      "tokens_per_step": world * MB * S,
+                      "step_ms": ms, "tokens_per_s": world * MB * S / (ms * 1e-3),
                       "ms_per_layer_incl_head": ms / n_layers, "activation_recompute": recompute,
                       "max_memory_gb": torch.cuda.max_memory_allocated(dev) / 1e9,
                       "losses": [round(l_["loss"], 4) for l_ in logs],
