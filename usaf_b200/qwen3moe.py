@@ -233,7 +233,7 @@ class _EPBlockFn(torch.autograd.Function):
             for c, p, nm in ((cg, gu, "gate_up_proj"), (cd, dn, "down_proj")):
                 if c is not None and p.n_ov != c.numel():
                     raise ValueError(f"{prefix}.{nm}: overlay and store hold different active sets")
-            if cg is None or cd is None:   # one vector missing: a zero-length stand-in
+            if cg is None or cd is None:   # the store wants one projection: the other's grads are discarded
                 cg = cg if cg is not None else torch.zeros(gu.n_ov, device=hs.device)
                 cd = cd if cd is not None else torch.zeros(dn.n_ov, device=hs.device)
         dx, dw_r = moe.backward(dy.contiguous(), hs, w_r, reduce_router=True, compact_gu=cg,
