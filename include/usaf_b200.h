@@ -217,9 +217,12 @@ int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w, const voi
  * every GPU that loads the library until exit); a projection with more
  * overlay coordinates returns USAF_EUNSUPPORTED.  The first call on a device
  * looks the array up (cudaGetSymbolAddress) with that device current, so make
- * that first call before any stream capture.  All calls share the one array:
- * calls that may overlap on the GPU (different streams, several threads)
- * race and must be serialized by the caller.  Allocates nothing. */
+ * that first call before any stream capture.  The looked-up address is kept
+ * for the life of the process and is not refreshed after cudaDeviceReset:
+ * do not call this entry point on a device after resetting it.  All calls
+ * share the one array: calls that may overlap on the GPU (different streams,
+ * several threads) race and must be serialized by the caller.  Allocates
+ * nothing. */
 int usaf_sparse_dw_noalloc(const usaf_route_plan *plan, const usaf_qweight *w, const void *gout,
                            const void *gin, int32_t dtype, const int32_t *csr_to_compact,
                            float scale, float *compact, void *stream);

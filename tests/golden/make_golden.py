@@ -202,16 +202,97 @@ def run_ties(ref_root):
     return {"seed": 7, "H": H, "E": E, "k": k, "T": T, "weights": seen["weights"]}
 
 
+def load_rigl_merge(ref_root):
+    """The per-tensor merge loop of train.py's ``do_reselect`` (train.py:552-596),
+    extracted with ``ast`` and run as it is written: the ``for fname, old in
+    active_idx.items():`` statement, executed in a namespace that provides the
+    names it reads (``active_idx``, ``new_idx``, ``masters``, ``q_dict``,
+    ``dequantize_4bit``) and collects the ones it writes (``_new_active``,
+    ``_new_masters``)."""
+    path = os.path.join(ref_root, "train.py")
+    tree = ast.parse(open(path).read())
+    fn = next(n for n in ast.walk(tree)
+              if isinstance(n, ast.FunctionDef) and n.name == "do_reselect")
+    loop = next(n for n in fn.body if isinstance(n, ast.For)
+                and isinstance(n.target, ast.Tuple)
+                and [e.id for e in n.target.elts] == ["fname", "old"])
+    mod = ast.Module(body=[loop], type_ignores=[])
+    ast.fix_missing_locations(mod)
+    return compile(mod, path, "exec")
+
+
+def run_rigl(ref_root):
+    """RigL merge known answers from the reference's own loop on C1-shaped
+    tensors.  Cases: (a) half of the new selection overlaps the old one;
+    (b) the new selection is smaller than the old one, so fewer coordinates
+    grow than were dropped; (c) no new selection (the tensor keeps its set)."""
+    from usaf.quantization import quantize_4bit as ref_quant, dequantize_4bit as ref_deq
+    code = load_rigl_merge(ref_root)
+    inp = make_block_inputs(**C1)
+    shapes = {"t.gate_up_proj": inp["gate_up_proj"]["shape"],
+              "t.down_proj": inp["down_proj"]["shape"],
+              "t.keep": inp["down_proj"]["shape"]}
+    g = torch.Generator().manual_seed(23)
+    active_idx, new_idx, masters, q_dict = {}, {}, {}, {}
+    sizes = {"t.gate_up_proj": (10485, 10485), "t.down_proj": (5242, 3000), "t.keep": (5242, 0)}
+    for fname, shape in shapes.items():
+        numel = int(np.prod(shape))
+        n_old, n_new = sizes[fname]
+        perm = torch.randperm(numel, generator=g)
+        old = perm[:n_old]
+        # half of the new selection from the old set, half from outside it
+        n_in = n_new // 2
+        new = torch.cat([old[torch.randperm(n_old, generator=g)[:n_in]],
+                         perm[n_old:n_old + n_new - n_in]])
+        new = new[torch.randperm(new.numel(), generator=g)]
+        active_idx[fname] = old
+        if n_new:
+            new_idx[fname] = new
+        masters[fname] = torch.nn.Parameter(torch.randn(n_old, generator=g) * 0.02,
+                                            requires_grad=False)
+        src = "gate_up_proj" if fname.endswith("gate_up_proj") else "down_proj"
+        w = torch.from_numpy(inp[src]["fp16"].astype(np.float32)) + 0.0
+        q, s, z, sh = ref_quant(w, 128)
+        q_dict[fname] = {"q": q, "s": s, "z": z, "shape": sh}
+    ns = {"torch": torch, "active_idx": active_idx, "new_idx": new_idx, "masters": masters,
+          "q_dict": q_dict, "dequantize_4bit": ref_deq, "_new_active": {}, "_new_masters": {},
+          "_n_kept": 0, "_n_dropped": 0, "_n_grown": 0}
+    exec(code, ns)
+    out = {"names": list(shapes)}
+    for fname in shapes:
+        out[f"{fname}.old"] = active_idx[fname].clone()
+        out[f"{fname}.new"] = new_idx[fname].clone() if fname in new_idx else None
+        out[f"{fname}.masters"] = masters[fname].detach().clone()
+        # the int4 entry is not stored: tests re-quantize the C1 dequant with the
+        # oracle's quantizer and check it against this hash
+        out[f"{fname}.qsz_sha"] = sha(q_dict[fname]["q"].numpy(), q_dict[fname]["s"].numpy(),
+                                      q_dict[fname]["z"].numpy())
+        out[f"{fname}.shape"] = tuple(q_dict[fname]["shape"])
+        out[f"{fname}.final"] = ns["_new_active"][fname].clone()
+        out[f"{fname}.final_masters"] = ns["_new_masters"][fname].detach().float().clone()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", default=None, help="comma list of fixtures to (re)write")
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
     torch.set_num_threads(os.cpu_count())
-    torch.save(run_case(a.reference, C1), os.path.join(HERE, "c1.pt"))
-    mini = dict(H=512, E=16, k=4, I=256, T=48, dtype=torch.bfloat16, seed=1, order="c2")
-    torch.save(run_case(a.reference, mini), os.path.join(HERE, "bf16_mini.pt"))
-    torch.save(run_ties(a.reference), os.path.join(HERE, "router_ties.pt"))
+    only = set(a.only.split(",")) if a.only else None
+
+    def want(name):
+        return only is None or name in only
+    if want("c1"):
+        torch.save(run_case(a.reference, C1), os.path.join(HERE, "c1.pt"))
+    if want("bf16_mini"):
+        mini = dict(H=512, E=16, k=4, I=256, T=48, dtype=torch.bfloat16, seed=1, order="c2")
+        torch.save(run_case(a.reference, mini), os.path.join(HERE, "bf16_mini.pt"))
+    if want("router_ties"):
+        torch.save(run_ties(a.reference), os.path.join(HERE, "router_ties.pt"))
+    if want("rigl"):
+        torch.save(run_rigl(a.reference), os.path.join(HERE, "rigl.pt"))
     print("golden fixtures written to", HERE)
 
 

@@ -206,8 +206,11 @@ def test_flow_vs_golden(dev, golden_dir, case):
 @pytest.mark.parametrize("case", ["c1", "bf16_mini"])
 def test_importance_selection_vs_golden(dev, golden_dir, case):
     """Selection from the CUDA importance pass: the same number of coordinates,
-    and any coordinate that differs from the reference's sits at the threshold
-    (its score is within the gradients' tolerance of the k-th score)."""
+    and every coordinate that differs from the reference's sits at a cut: its
+    score is within the gradients' tolerance of the global k-th score or of
+    its expert's candidate cut (the per-expert top-``2*frac`` of
+    usaf/moe_loader.py:604-611).  Reference scores come from the fixture's
+    candidate lists, device scores from the device store."""
     from usaf_b200.layer import SparseMoELayer
     cfg = C1 if case == "c1" else MINI
     g = torch.load(os.path.join(golden_dir, f"{case}.pt"), weights_only=False)
@@ -217,12 +220,56 @@ def test_importance_selection_vs_golden(dev, golden_dir, case):
                            inp["k"], inp["T"], True, PREFIX)
     store = layer.importance(inp["x"].to(dev).contiguous(), inp["dy"].to(dev).contiguous(), 0.005)
     sel = store.select(0.005)
+    tol = 1e-5 if cfg["dtype"] == torch.float32 else 1e-2
     for n in (GU, DN):
         ref = g[f"active.{n}"]
         got = sel[n].cpu()
         assert got.numel() == ref.numel()
-        overlap = len(set(got.tolist()) & set(ref.tolist())) / ref.numel()
-        assert overlap > (0.999 if cfg["dtype"] == torch.float32 else 0.98), overlap
+        numel_e = int(np.prod(p[n.rsplit(".", 1)[1]].shape[1:]))
+        # score maps and cuts, reference side and device side
+        r_vals, r_idx = g[f"cand.{n}.vals"].float(), g[f"cand.{n}.idx"].long()
+        d_vals, d_idx = (t.cpu() for t in store.candidate_list(n))
+        d_vals, d_idx = d_vals.float(), d_idx.long()
+        sides = {"reference": (r_vals, r_idx, ref.long()), "device": (d_vals, d_idx, got.long())}
+        cuts = {}
+        for side, (vals, idx, chosen) in sides.items():
+            score = dict(zip(idx.tolist(), vals.tolist()))
+            kth = min(score[c] for c in chosen.tolist())
+            per_e = {}
+            for c, v in zip(idx.tolist(), vals.tolist()):
+                e = c // numel_e
+                per_e[e] = min(per_e.get(e, float("inf")), v)
+            cuts[side] = (score, kth, per_e)
+        only = {"reference": sorted(set(ref.tolist()) - set(got.tolist())),
+                "device": sorted(set(got.tolist()) - set(ref.tolist()))}
+        bad = []
+        for side, coords in only.items():
+            score, kth, per_e = cuts[side]
+            for c in coords:
+                v = score[c]
+                near_kth = abs(v - kth) <= tol * kth
+                near_cut = abs(v - per_e[c // numel_e]) <= tol * per_e[c // numel_e]
+                if not (near_kth or near_cut):
+                    bad.append((side, c, v, kth, per_e[c // numel_e]))
+        n_diff = len(only["reference"])
+        assert not bad, f"{n}: {len(bad)} of {n_diff} differing coordinates are not at a cut: {bad[:10]}"
+        assert n_diff <= (0.001 if cfg["dtype"] == torch.float32 else 0.02) * ref.numel(), n_diff
+
+
+def logit_flips(got_w, ref_w, ref_logits, k):
+    """Tokens whose routing masks differ, with the reference's k-th and
+    (k+1)-th largest bf16 logits and the bound a flip must respect: two
+    logits that each carry at most one bf16 rounding of difference can only
+    swap order (or tie) when they are within 2 ulp of each other."""
+    flips = []
+    tok = ((got_w != 0) != (ref_w != 0)).any(1).nonzero().reshape(-1).tolist()
+    for t in tok:
+        l = ref_logits[t].float().sort(descending=True).values
+        a, b = l[k - 1].item(), l[k].item()
+        mag = max(abs(a), abs(b), 2 ** -126)
+        ulp = 2.0 ** (np.floor(np.log2(mag)) - 7)
+        flips.append({"token": t, "kth": a, "next": b, "gap": a - b, "bound": 2 * ulp})
+    return flips
 
 
 def test_c2_shapes_vs_oracle(dev):
@@ -255,10 +302,70 @@ def test_c2_shapes_vs_oracle(dev):
     store = omoe.SparseGradStore(active, shapes)
     ref = omoe.block_step(x, w_r, w_gu, w_dn, inp["dy"], k, True, capture=store.add,
                           prefix=PREFIX, experts="sparse")
-    mism = (out["weights"] != 0) != (ref["weights"] != 0)
-    assert mism.sum().item() <= T * E * 1e-3, "routing masks differ beyond logit-rounding flips"
-    close(out["y"], ref["y"], 2e-2, "y")
-    close(out["dX"], ref["dX"], 2e-2, "dX")
+    flips = logit_flips(out["weights"], ref["weights"], ref["logits"], k)
+    print(f"routing flips ({len(flips)} of {T} tokens):", flips)
+    wide = [f for f in flips if f["gap"] > f["bound"]]
+    assert not wide, f"routing differs on tokens whose k-th/(k+1)-th logit gap exceeds 2 bf16 ulp: {wide}"
+    keep = torch.ones(T, dtype=torch.bool)
+    keep[[f["token"] for f in flips]] = False
+    close(out["y"][keep], ref["y"][keep], 2e-2, "y")
+    close(out["dX"][keep], ref["dX"][keep], 2e-2, "dX")
+    close(out["dW_r"], ref["dW_r"], 2e-2, "dW_r")
+    for n in (GU, DN):
+        close(out["compact"][n], store.compact[n], 2e-2, f"compact {n}")
+
+
+def test_c2_full_step_vs_oracle(dev):
+    """The benched configuration itself: one C2 layer (T 4096, H 2048, E 128,
+    k 8, I 768, bf16), overlay chosen by the device importance pass (rows with
+    hundreds of trained coordinates), one train_step against the oracle's
+    sparse-dispatch block on the same int4 weights and active set.  Routing
+    flips are listed and must sit within 2 bf16 ulp of a logit tie; y and dX
+    are compared on the other tokens."""
+    from usaf_b200.engine import Projection
+    from usaf_b200.layer import SparseMoELayer
+    from usaf_b200.quantization import quantize_4bit
+    from oracle.flow import dense_weights
+    H, E, k, I, T = 2048, 128, 8, 768, 4096
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    w_r = (torch.randn(E, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    dy = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    inp = {"H": H, "E": E, "k": k, "I": I, "T": T, "dtype": torch.bfloat16,
+           "x": x.cpu(), "w_r": w_r.cpu(), "dy": dy.cpu()}
+    proj = {}
+    for n, shape in (("gate_up_proj", (E, 2 * I, H)), ("down_proj", (E, H, I))):
+        w = torch.randn(*shape, device=dev, generator=g) * 0.02
+        q, s, z, _ = quantize_4bit(w, 128)
+        del w
+        proj[n] = Projection(q, s, z, shape, 128, torch.bfloat16)
+        # the device dequant is bit-exact with the oracle's (test_dequant_expert_tensor_bitexact)
+        inp[n] = {"shape": shape, "fp16": proj[n].dequant(torch.float16).cpu().numpy()}
+    layer = SparseMoELayer(w_r.clone(), proj["gate_up_proj"], proj["down_proj"], k, T, True, PREFIX)
+    active = {n: a.cpu() for n, a in layer.importance(x, dy, 0.005).select(0.005).items()}
+    layer.init_selection({n: a.to(dev) for n, a in active.items()}, lr=1e-4)
+    y, dx, dw_r = layer.train_step(x, dy)
+    torch.cuda.synchronize()
+    layer.block.check()
+    out = {"y": y.cpu(), "dX": dx.cpu(), "dW_r": dw_r.cpu(), "weights": layer.block.weights.cpu(),
+           "compact": {n: layer.reorder_to(n, layer.store.compact[n], active[n].to(dev)).cpu()
+                       for n in active}}
+    masters = {n: torch.from_numpy(inp[n.rsplit(".", 1)[1]]["fp16"].reshape(-1)[active[n].numpy()]).float()
+               for n in active}
+    w_gu, w_dn = dense_weights(inp, {n: (active[n], masters[n]) for n in active})
+    shapes = {GU: (E, 2 * I, H), DN: (E, H, I)}
+    store = omoe.SparseGradStore(active, shapes)
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    ref = omoe.block_step(inp["x"], inp["w_r"], w_gu, w_dn, inp["dy"], k, True, capture=store.add,
+                          prefix=PREFIX, experts="sparse")
+    flips = logit_flips(out["weights"], ref["weights"], ref["logits"], k)
+    print(f"C2 routing flips ({len(flips)} of {T} tokens):", flips)
+    wide = [f for f in flips if f["gap"] > f["bound"]]
+    assert not wide, f"routing differs on tokens whose k-th/(k+1)-th logit gap exceeds 2 bf16 ulp: {wide}"
+    keep = torch.ones(T, dtype=torch.bool)
+    keep[[f["token"] for f in flips]] = False
+    close(out["y"][keep], ref["y"][keep], 2e-2, "y")
+    close(out["dX"][keep], ref["dX"][keep], 2e-2, "dX")
     close(out["dW_r"], ref["dW_r"], 2e-2, "dW_r")
     for n in (GU, DN):
         close(out["compact"][n], store.compact[n], 2e-2, f"compact {n}")

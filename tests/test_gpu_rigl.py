@@ -49,3 +49,40 @@ def test_merge_vs_oracle(dev, case):
                                    masters.to(dev), orig.to(dev))
     assert torch.equal(got_idx.cpu().long(), ref_idx.long())
     assert torch.equal(got_vals.cpu().float(), ref_vals.float())
+
+
+def _fixture_case(golden_dir, fname):
+    """Inputs of one tensor of the reference-generated RigL fixture; the int4
+    entry is the C1 dequant re-quantized (checked against the fixture's hash)."""
+    import os
+    import numpy as np
+    from oracle import quant as oquant
+    from oracle.inputs import C1, make_block_inputs
+    import hashlib
+
+    def sha(*arrays):
+        h = hashlib.sha256()
+        for a in arrays:
+            h.update(np.ascontiguousarray(a).tobytes())
+        return h.hexdigest()
+    g = torch.load(os.path.join(golden_dir, "rigl.pt"), weights_only=False)
+    inp = make_block_inputs(**C1)
+    src = "gate_up_proj" if fname.endswith("gate_up_proj") else "down_proj"
+    q, s, z, shape = oquant.quantize_4bit(inp[src]["fp16"].astype(np.float32), 128)
+    assert sha(q, s, z) == g[f"{fname}.qsz_sha"]
+    orig = torch.from_numpy(oquant.dequantize_4bit(q, s, z, shape, 128)).reshape(-1)
+    return g, orig
+
+
+@pytest.mark.parametrize("fname", ["t.gate_up_proj", "t.down_proj", "t.keep"])
+def test_merge_vs_reference_fixture(dev, golden_dir, fname):
+    """usaf_b200.rigl.merge against the reference's own merge loop
+    (train.py:552-596, run by tests/golden/make_golden.py): identical final
+    index list (kept then grown, each ascending) and identical values."""
+    from usaf_b200 import rigl
+    g, orig = _fixture_case(golden_dir, fname)
+    new = g[f"{fname}.new"]
+    got_idx, got_vals = rigl.merge(g[f"{fname}.old"].to(dev), None if new is None else new.to(dev),
+                                   g[f"{fname}.masters"].to(dev), orig.to(dev))
+    assert torch.equal(got_idx.cpu().long(), g[f"{fname}.final"].long())
+    assert torch.equal(got_vals.cpu().float(), g[f"{fname}.final_masters"])

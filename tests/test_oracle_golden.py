@@ -144,3 +144,19 @@ def test_rigl_merge_known_answer():
     final, vals = moe.rigl_merge(old, new, masters, orig)
     assert final.tolist() == [5, 9, 1, 3]
     assert vals.tolist() == [50.0, 90.0, 0.5, 1.5]
+
+
+@pytest.mark.parametrize("fname", ["t.gate_up_proj", "t.down_proj", "t.keep"])
+def test_rigl_merge_matches_reference_fixture(golden_dir, fname):
+    """The oracle's merge against the reference's own loop (train.py:552-596,
+    extracted with ast and run by tests/golden/make_golden.py)."""
+    g = load(golden_dir, "rigl.pt")
+    inp = make_block_inputs(**C1)
+    src = "gate_up_proj" if fname.endswith("gate_up_proj") else "down_proj"
+    q, s, z, shape = quant.quantize_4bit(inp[src]["fp16"].astype(np.float32), 128)
+    assert sha(q, s, z) == g[f"{fname}.qsz_sha"]
+    orig = torch.from_numpy(quant.dequantize_4bit(q, s, z, shape, 128)).reshape(-1)
+    new = g[f"{fname}.new"]
+    final, vals = moe.rigl_merge(g[f"{fname}.old"], new, g[f"{fname}.masters"], orig)
+    assert torch.equal(final.long(), g[f"{fname}.final"].long())
+    assert torch.equal(vals.float(), g[f"{fname}.final_masters"])

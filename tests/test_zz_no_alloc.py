@@ -28,11 +28,14 @@ def rel(a, b):
     return ((a.double() - b.double()).norm() / b.double().norm().clamp_min(1e-30)).item()
 
 
-def test_noalloc_matches_scratch_entry_point(dev):
+# T=512: the tensor-core kernel; T=64: at most 64 pair slots per expert
+# (P_cap = 64 * 8 = 512 <= 64 * E), the CUDA-core kernel
+@pytest.mark.parametrize("T", [512, 64])
+def test_noalloc_matches_scratch_entry_point(dev, T):
     from usaf_b200 import _lib
     from usaf_b200.engine import BlockDims, MoEBlock, Projection
     from usaf_b200.quantization import quantize_4bit
-    T, H, E, k, I = 512, 512, 16, 4, 256
+    H, E, k, I = 512, 16, 4, 256
     g = torch.Generator(device=dev).manual_seed(11)
     x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
     dy = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
@@ -46,6 +49,7 @@ def test_noalloc_matches_scratch_entry_point(dev):
         p.set_overlay(idx, torch.randn(idx.numel(), device=dev, generator=g) * 0.02)
         proj[n] = p
     blk = MoEBlock(BlockDims(T, H, E, I, k, True, torch.bfloat16), dev)
+    assert (blk.P_cap <= 64 * E) == (T == 64)
     blk.forward(x, w_r, proj["gate_up_proj"], proj["down_proj"])
     blk.backward(dy, x, w_r, proj["gate_up_proj"], proj["down_proj"])
     st = _lib.stream()

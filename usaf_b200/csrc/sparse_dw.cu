@@ -14,6 +14,7 @@
 // (the block's rows) are staged transposed in shared memory so every
 // coordinate reads contiguous token runs; per-chunk partial sums go to an
 // fp32 scratch vector owned one-to-one by coordinates (no atomics).
+#include <atomic>
 #include "common.cuh"
 
 namespace usaf {
@@ -291,26 +292,33 @@ static __device__ __align__(256) float g_sddmm_noalloc_scratch[usaf::kNoAllocScr
 
 // Device address of the scratch array on the current device.  The host-side
 // symbol is only a stand-in, so the address is looked up once per device
-// (with that device current) and cached.
+// (with that device current) and cached.  The cache entries are atomics:
+// host threads that make their first call on a device at the same time may
+// each look the address up, and they all store the same value.  The cache is
+// not refreshed after cudaDeviceReset (the library's module, and with it the
+// array, is loaded again at a possibly different address): a process that
+// resets a device must not call this entry point on it afterwards.
 static float *noalloc_scratch_ptr(int *status) {
     constexpr int kMaxDevices = 64;
-    static float *addr[kMaxDevices] = {};
+    static std::atomic<float *> addr[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         *status = USAF_ECUDA;
         return nullptr;
     }
-    if (!addr[dev]) {
+    float *cached = addr[dev].load(std::memory_order_acquire);
+    if (!cached) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_sddmm_noalloc_scratch) != cudaSuccess || !p) {
             (void)cudaGetLastError();
             *status = USAF_ECUDA;
             return nullptr;
         }
-        addr[dev] = static_cast<float *>(p);
+        cached = static_cast<float *>(p);
+        addr[dev].store(cached, std::memory_order_release);
     }
     *status = USAF_OK;
-    return addr[dev];
+    return cached;
 }
 
 extern "C" int usaf_sparse_dw_noalloc(const usaf_route_plan *plan, const usaf_qweight *w,

@@ -55,7 +55,14 @@ class SparseMoELayer:
         return store
 
     def init_selection(self, active: Dict[str, torch.Tensor], lr=1e-4, weight_decay=0.01,
-                       router_lr=None):
+                       router_lr=None, router_optimizer: str = "adam"):
+        """Masters from the original int4 dequant at ``active``, overlays,
+        capture store and the optimizers.  ``router_optimizer``: ``"adam"``
+        steps the router with SparseAdam over all of W_r (the C2
+        configuration); ``"sgd"`` with train.py's SGD, momentum 0.9 and the
+        same weight decay (train.py:494-498, 667-672)."""
+        if router_optimizer not in ("adam", "sgd"):
+            raise ValueError(f"router_optimizer must be 'adam' or 'sgd', got {router_optimizer!r}")
         # compact vectors (masters, moments, gradients) in CSR order: the kernels'
         # compact <-> overlay maps become the identity (streaming accesses)
         self.active = {n: a.reshape(-1).long() for n, a in active.items()}
@@ -78,10 +85,16 @@ class SparseMoELayer:
         rname = self.prefix.replace(".experts", ".gate.weight")
         self.router_name = rname
         self.router_param = torch.nn.Parameter(self.w_r, requires_grad=False)
-        self.router_opt = SparseAdam({rname: self.router_param},
-                                     active_idx={rname: torch.arange(E * H, device=self.w_r.device)},
-                                     lr=router_lr if router_lr is not None else lr,
-                                     weight_decay=weight_decay)
+        rlr = router_lr if router_lr is not None else lr
+        self.router_sgd = None
+        if router_optimizer == "sgd":
+            self.router_opt = None
+            self.router_sgd = torch.optim.SGD([self.router_param], lr=rlr, momentum=0.9,
+                                              weight_decay=weight_decay)
+        else:
+            self.router_opt = SparseAdam({rname: self.router_param},
+                                         active_idx={rname: torch.arange(E * H, device=self.w_r.device)},
+                                         lr=rlr, weight_decay=weight_decay)
 
     def train_step(self, x, dy, loss_scale: float = 1.0, accum: int = 1, micro=None):
         """One optimizer step over ``accum`` micro-batches (x, dy pairs)."""
@@ -98,7 +111,12 @@ class SparseMoELayer:
         denom = float(loss_scale * accum)
         self.opt.step(compact_grads=self.store.compact, grad_div=denom)
         self.router_param.grad = dw_r_acc
-        self.router_opt.step(grad_div=denom)
+        if self.router_sgd is not None:
+            # train.py:667-671: the gradient is divided in place, then SGD steps
+            dw_r_acc.div_(denom)
+            self.router_sgd.step()
+        else:
+            self.router_opt.step(grad_div=denom)
         self.router_param.grad = None
         return out
 

@@ -126,13 +126,19 @@ def _block_for(owner, T: int, H: int, E: int, I: int, top_k: int, norm: bool, dt
 
 def _ep_for(owner, T: int, w_r: torch.Tensor, top_k: int, norm: bool, gu: Projection,
             dn: Projection, group):
-    """Expert-parallel workspace of one module for T tokens (one per module)."""
+    """Expert-parallel workspace of one module for T tokens (one per module).
+
+    The key holds everything the workspace is built from: the pair factor in
+    force, and the projections themselves (re-attaching other int4 weights
+    builds a new workspace instead of reusing one bound to the old ones; the
+    cached workspace keeps its projections alive, so their ids stay unique)."""
     from .expert_parallel import ExpertParallelMoE
     cache = owner.__dict__.setdefault("_usaf_ep_moes", {})
-    key = (T, top_k, norm)
+    pf = _POLICY["pair_factor"]
+    key = (T, top_k, norm, pf, id(gu), id(dn), id(group))
     moe = cache.get(key)
     if moe is None:
-        moe = ExpertParallelMoE(w_r, gu, dn, top_k, T, norm, group, _POLICY["pair_factor"])
+        moe = ExpertParallelMoE(w_r, gu, dn, top_k, T, norm, group, pf)
         cache[key] = moe
     return moe
 

@@ -28,7 +28,9 @@ weights from :func:`usaf_b200.qwen3moe.attach_int4_experts`):
   per-tensor top-k over all ranks' candidates (the single-process selection
   over the union of the ranks' batches), the router gradient is summed over
   the ranks, and every rank takes the same skip / raise decision; each rank
-  saves its own checkpoint file.
+  saves its own checkpoint file.  A step over W ranks with ``accum``
+  micro-batches each is one process accumulating ``accum * W`` micro-batches:
+  the summed gradients are divided by ``loss_scale * accum * W``.
 
 Everything stays on the device; one host read per step carries the
 finiteness flag, the loss and the error words of the block workspaces (a
@@ -182,9 +184,7 @@ class SparseTrainer:
             vals, idxs = store.candidate_list(name, device=dev)
             k = max(1, int(math.prod(shape) * self.frac))
             g = global_select(vals, idxs, k, self.ep_group)
-            span = math.prod(self.shapes[name])
-            lo = self.ep_rank * span
-            out[name] = g[(g >= lo) & (g < lo + span)] - lo
+            out[name] = shard_share(g, self.ep_rank, math.prod(self.shapes[name]))
         return out
 
     def _clear_capture(self) -> None:
@@ -258,20 +258,18 @@ class SparseTrainer:
         for mb in micro_batches:
             loss_sum += self._backward(loss_fn, mb)
         scale = self.scaler.scale
-        denom = scale * self.accum
+        # train.py:661-662 divides the summed gradients by loss_scale * ACCUM.  Under
+        # expert parallelism every shard's gradient (and the all-reduced router
+        # gradient) sums W ranks' micro-batches, each with a loss averaged over its
+        # own tokens: one step is one process accumulating accum * W micro-batches
+        denom = scale * self.accum * (dist.get_world_size(self.ep_group) if self.expert_parallel else 1)
         # train.py:662-663: the step runs only if every expert gradient is finite
         flags = torch.stack([torch.isfinite(g).all() for g in self.store.compact.values()])
         blocks = qwen3moe.workspaces(self.model)
         nf = flags.numel()
         dev_vals = torch.cat([flags.float(), loss_sum.reshape(1)] + [b.err.float() for b in blocks])
         if self.expert_parallel:
-            # every rank takes the same decision: skip if any shard is non-finite, raise if
-            # any rank's workspace flagged an error; the logged loss is the ranks' mean
-            agg = torch.cat([(1.0 - dev_vals[:nf]), dev_vals[nf:nf + 1],
-                             (dev_vals[nf + 1:] != 0).float().sum().reshape(1)])
-            dist.all_reduce(agg, group=self.ep_group)
-            W = dist.get_world_size(self.ep_group)
-            dev_vals = torch.cat([(agg[:nf] == 0).float(), agg[nf:nf + 1] / W, agg[nf + 1:]])
+            dev_vals = ranks_agree(dev_vals, nf, self.ep_group)
         host = dev_vals.cpu()
         if bool(host[nf + 1:].any()):
             for b in blocks:
@@ -317,6 +315,30 @@ class SparseTrainer:
             self.scaler.load_state_dict(cfg)
         lr = lr_at(max(self.step_num, 1), self.steps, self.lr_peak)
         self.init_selection(st["active_idx"], st["masters"], lr=lr, optimizer_state=st["optimizer"])
+
+
+def shard_share(g: torch.Tensor, rank: int, span: int) -> torch.Tensor:
+    """This rank's part of a global selection ``g`` (flat indices of the full
+    [E, R, C] tensor) as flat indices of its shard: rank r owns the flat
+    range [r * span, (r + 1) * span), span = (E / W) * R * C."""
+    lo = rank * span
+    return g[(g >= lo) & (g < lo + span)] - lo
+
+
+def ranks_agree(dev_vals: torch.Tensor, nf: int, group=None) -> torch.Tensor:
+    """One decision for all ranks of an expert-parallel step.
+
+    ``dev_vals`` = ``nf`` finiteness flags (1 = finite) of this rank's expert
+    gradients, the rank's summed loss, then the error words of its block
+    workspaces.  Returns the same layout: a flag is 1 only if it is 1 on
+    every rank (a non-finite shard skips the step everywhere), the loss is
+    the ranks' mean, and the last entry counts the nonzero error words over
+    all ranks (any of them makes every rank raise)."""
+    agg = torch.cat([(1.0 - dev_vals[:nf]), dev_vals[nf:nf + 1],
+                     (dev_vals[nf + 1:] != 0).float().sum().reshape(1)])
+    dist.all_reduce(agg, group=group)
+    W = dist.get_world_size(group)
+    return torch.cat([(agg[:nf] == 0).float(), agg[nf:nf + 1] / W, agg[nf + 1:]])
 
 
 def _permute_state(sd: dict, name: str, perm: torch.Tensor) -> dict:
