@@ -134,15 +134,65 @@ def experts_sparse_loop(hs, weights, w_gu, w_dn, capture: Optional[CaptureFn] = 
     return final.to(hs.dtype)
 
 
+def experts_batched(hs, weights, w_gu, w_dn, capture: Optional[CaptureFn] = None,
+                    prefix: str = ""):
+    """``batched_sparse_experts_forward`` (benchmarks/kaggle_t4_bench.py:284-328).
+
+    The routed pairs are grouped by expert (the dispatch of
+    :func:`dispatch_indices`) into a zero-padded ``[E, cap, H]`` batch, cap =
+    the largest expert count; two ``bmm`` run every expert at once; the
+    weighted rows are ``index_add``-ed into an fp32 output (padding rows carry
+    weight 0).  Capture: one hook per stacked weight tensor hands each
+    expert's slice of the ``[E, *, *]`` gradient to ``capture`` (:310-318).
+    """
+    N, Hd = hs.shape
+    E = w_gu.shape[0]
+    tok_idx, exp_idx = torch.nonzero(weights, as_tuple=True)             # :293
+    if tok_idx.numel() == 0:
+        return torch.zeros(N, Hd, dtype=hs.dtype)
+    counts = torch.bincount(exp_idx, minlength=E)
+    cap = int(counts.max().item())
+    order = torch.argsort(exp_idx, stable=True)
+    exp_s, tok_s = exp_idx[order], tok_idx[order]
+    offs = torch.zeros(E, dtype=torch.long)
+    offs[1:] = torch.cumsum(counts, 0)[:-1]
+    pos = torch.arange(exp_s.numel()) - offs[exp_s]
+    pad_tok = torch.zeros(E, cap, dtype=torch.long)
+    pad_w = torch.zeros(E, cap, dtype=weights.dtype)
+    pad_tok[exp_s, pos] = tok_s
+    pad_w[exp_s, pos] = weights[tok_s, exp_s]                            # :306-307
+    x_b = hs[pad_tok]                                                    # :309
+    wg, wd = w_gu.detach(), w_dn.detach()
+    if capture is not None and torch.is_grad_enabled():
+        def _all(name):
+            def h(g):
+                for ei in range(E):
+                    capture(name, ei, g[ei])
+            return h
+        wg.requires_grad_(True)
+        wd.requires_grad_(True)
+        wg.register_hook(_all(prefix + ".gate_up_proj"))
+        wd.register_hook(_all(prefix + ".down_proj"))
+    gu = torch.bmm(x_b, wg.transpose(1, 2))                              # :319
+    gate, up = gu.chunk(2, dim=-1)
+    cur = F.silu(gate) * up
+    cur = torch.bmm(cur, wd.transpose(1, 2))                             # :322
+    cur = cur.float() * pad_w.float().unsqueeze(-1)
+    final = torch.zeros(N, Hd, dtype=torch.float32)
+    final = final.index_add(0, pad_tok.reshape(-1), cur.reshape(-1, Hd))  # :325-326
+    return final.to(hs.dtype)
+
+
 def block_step(hs, w_r, w_gu, w_dn, dY, top_k: int, norm_topk_prob: bool = True,
                capture: Optional[CaptureFn] = None, prefix: str = "layer",
                experts: str = "sparse"):
     """One forward + backward of the MoE block with router co-training.
 
     Forward = ``dml_qwen3_moe_block_forward`` (usaf/qwen3moe_dml.py:67-86)
-    with the experts computed either dense-masked (:24-64, ``experts="dense"``)
-    or by the reference's per-expert sparse loop
-    (benchmarks/kaggle_t4_bench.py:253-282, ``experts="sparse"``); backward
+    with the experts computed dense-masked (:24-64, ``experts="dense"``), by
+    the reference's per-expert sparse loop (benchmarks/kaggle_t4_bench.py:
+    253-282, ``experts="sparse"``) or by its batched dispatch (:284-328,
+    ``experts="batched"``); backward
     is ``y.backward(dY)`` through both, as the recompute-backward of
     train.py:356-364 does for one layer.  Expert gradients go to ``capture``;
     the router gradient and dX are returned.
@@ -150,7 +200,8 @@ def block_step(hs, w_r, w_gu, w_dn, dY, top_k: int, norm_topk_prob: bool = True,
     hs = hs.detach().clone().requires_grad_(True)
     w_r = w_r.detach().clone().requires_grad_(True)
     logits, probs, mask, weights = router_forward(hs, w_r, top_k, norm_topk_prob)
-    fn = experts_dense_masked if experts == "dense" else experts_sparse_loop
+    fn = {"dense": experts_dense_masked, "sparse": experts_sparse_loop,
+          "batched": experts_batched}[experts]
     y = fn(hs, weights, w_gu, w_dn, capture=capture, prefix=prefix)
     y.backward(dY)
     return {"y": y.detach(), "dX": hs.grad.detach(), "dW_r": w_r.grad.detach(),

@@ -160,3 +160,27 @@ def test_rigl_merge_matches_reference_fixture(golden_dir, fname):
     final, vals = moe.rigl_merge(g[f"{fname}.old"], new, g[f"{fname}.masters"], orig)
     assert torch.equal(final.long(), g[f"{fname}.final"].long())
     assert torch.equal(vals.float(), g[f"{fname}.final_masters"])
+
+
+def test_flow_batched_dispatch_matches_reference(case):
+    """The oracle's restatement of the batched dispatch
+    (benchmarks/kaggle_t4_bench.py:284-328, the CPU baseline's fast path):
+    its output equals the reference function's own output on the same routing
+    (the fixture ran the extracted reference function), and its training pass
+    on the reference's active set agrees with the dense-masked reference
+    within the float tolerance."""
+    from oracle.flow import dense_weights, masters_of, shapes_of
+    name, cfg, g, inp = case
+    active = {n: g[f"active.{n}"] for n in (GU, DN)}
+    masters = masters_of(inp, active)
+    w_gu, w_dn = dense_weights(inp, {n: (active[n], masters[n]) for n in active})
+    store = moe.SparseGradStore(active, shapes_of(inp))
+    out = moe.block_step(inp["x"], inp["w_r"], w_gu, w_dn, inp["dy"], inp["k"], True,
+                         capture=store.add, prefix=PREFIX, experts="batched")
+    tol = 1e-5 if cfg["dtype"] == torch.float32 else 2e-2
+    assert torch.equal(out["weights"], g["weights"])
+    assert torch.equal(out["y"], g["y_batched"])
+    assert rel(out["dX"], g["dX"]) < tol
+    assert rel(out["dW_r"], g["dW_r"]) < tol
+    for n in (GU, DN):
+        assert rel(store.compact[n], g[f"compact.{n}"]) < tol

@@ -10,8 +10,9 @@
 //     never touch shared memory or HBM;
 //   * B (tokens of the expert's segment, K-major) arrives in shared memory by
 //     TMA with the 128-byte swizzle (plain per-CTA loads, no multicast);
-//   * one thread issues tcgen05.mma (kind::f16, M=128, N<=128 per sub-tile,
-//     A from TMEM, B from SMEM) into fp32 TMEM accumulators; tcgen05.commit
+//   * one thread issues tcgen05.mma (kind::f16, M=128, N<=256 for the first
+//     256 tokens and N<=128 for the rest, A from TMEM, B from SMEM) into fp32
+//     TMEM accumulators; tcgen05.commit
 //     frees pipeline stages and finally signals the epilogue;
 //   * the epilogue warps read the accumulators (tcgen05.ld), round to bf16,
 //     transpose through shared memory and write token rows with 16-byte
@@ -22,10 +23,12 @@
 #include <cudaTypedefs.h>
 
 #include "gemm_tc.cuh"
+#include "gemm_tc_dev.cuh"
 #include "tc_common.cuh"
 
 namespace usaf {
 using namespace tc;
+using namespace gemm_dev;
 
 namespace {
 
@@ -59,119 +62,6 @@ constexpr size_t kSzBytes = (size_t)4 * kBK * 4;          // transposed-mode sca
 // stages + epilogue staging + scale ring + shared block + tile prefix / counts (E <= 1024)
 constexpr size_t kSmemBytes =
     (size_t)kStages * kStageBytes + kStgBytes + kSzBytes + sizeof(TcShared) + 8 * 1025 + 1024;
-
-// time-bounded wait that ignores the abort flag (used to drain in-flight work)
-__device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity, int *err) {
-    uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > kWaitBudgetNs) {
-            atomicOr(err, USAF_ERR_WAIT_TIMEOUT);
-            return;
-        }
-    }
-}
-
-// Dequantize 32 elements (16 pairs) from 4 code words in the repacked
-// order: pair i = nibbles (i%4, i%4+4) of word i/4.  fp16(fp16(q*s)+z) per
-// element (separately rounded multiply and add, the reference's rounding),
-// then bf16.  SCALE_PER_ROW: pair i has its own (scale, zero) per element
-// (transposed weights); otherwise one (scale, zero) for the whole block.
-// A pending trained coordinate at pair pj is blended in after the bf16
-// conversion (sel picks the half).
-template <bool SCALE_PER_ROW>
-__device__ __forceinline__ void dequant16(uint4 codes, uint32_t szw, const uint32_t *szr, int pj,
-                                          uint32_t m2, uint32_t sel, uint32_t (&r)[16]) {
-    const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
-    const __half2 magic = __half2half2(__ushort_as_half((unsigned short)0x6400));
-    __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFF)));
-    __half2 z2 = __half2half2(__ushort_as_half((unsigned short)(szw >> 16)));
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        uint32_t u = ((w[i >> 2] >> (4 * (i & 3))) & 0x000F000Fu) | 0x64006400u;
-        __half2 c = __hsub2(*reinterpret_cast<__half2 *>(&u), magic);
-        if (SCALE_PER_ROW) {
-            uint32_t wa = szr[2 * i], wb = szr[2 * i + 1];
-            uint32_t su = __byte_perm(wa, wb, 0x5410), zu = __byte_perm(wa, wb, 0x7632);
-            s2 = *reinterpret_cast<__half2 *>(&su);
-            z2 = *reinterpret_cast<__half2 *>(&zu);
-        }
-        __half2 v = __hadd2_rn(__hmul2_rn(c, s2), z2);
-        float2 f = __half22float2(v);
-        __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
-        uint32_t rv = *reinterpret_cast<uint32_t *>(&bb);
-        r[i] = (i == pj) ? __byte_perm(rv, m2, sel) : rv;
-    }
-}
-
-// slow path for a second trained coordinate in the same 32-wide block:
-// predicated select per register keeps r[] in registers
-__device__ __forceinline__ void patch_elem16(uint32_t (&r)[16], int c, uint32_t vb) {
-    const uint32_t pi = (uint32_t)c >> 1;
-    const bool hi = c & 1;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const uint32_t cand = hi ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
-        asm volatile("{\n .reg .pred p;\n setp.eq.u32 p, %1, %2;\n selp.b32 %0, %3, %0, p;\n}\n"
-                     : "+r"(r[i])
-                     : "r"(pi), "r"((uint32_t)i), "r"(cand));
-    }
-}
-
-// packed fp32 pairs (sm_100 f32x2 arithmetic, round to nearest even)
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
-}
-__device__ __forceinline__ float f2_lo(uint64_t a) { return __uint_as_float((uint32_t)a); }
-__device__ __forceinline__ float f2_hi(uint64_t a) { return __uint_as_float((uint32_t)(a >> 32)); }
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-    uint64_t d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-// bf16 pair (low half = first element) <-> packed fp32 pair
-__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t w) {
-    return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-}
-__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t a) {
-    const __nv_bfloat162 r = __floats2bfloat162_rn(f2_lo(a), f2_hi(a));
-    return *reinterpret_cast<const uint32_t *>(&r);
-}
-
-__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-        : "memory");
-}
-
-__device__ __forceinline__ void decode_tile(const int *tile_off, const int *cnts, int E, int tile,
-                                            int &e, int &t0, int &ntok) {
-    int lo = 0, hi = E;  // first expert with tile_off[e+1] > tile
-    while (lo < hi) {
-        int mid = (lo + hi) >> 1;
-        if (tile_off[mid + 1] > tile) hi = mid;
-        else lo = mid + 1;
-    }
-    e = lo;
-    int cnt = cnts[e];
-    int ntt = tile_off[e + 1] - tile_off[e];
-    int tt = tile - tile_off[e];
-    int per = (((cnt + ntt - 1) / ntt) + 15) & ~15;
-    t0 = tt * per;
-    ntok = min(per, cnt - t0);
-}
 
 // MODE_GATE_UP : rows = 64 gate + 64 up storage rows, K = C, SwiGLU epilogue
 //                (out0 = gu [P,R], out1 = h [P,R/2])
@@ -290,10 +180,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int work = blockIdx.x; work < n_work && !*abort_flag; work += gridDim.x, ++it) {
                 int e, t0, ntok;
                 decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
-                const int nsub = (ntok + kSub - 1) / kSub;
-                const int n0 = min(kSub, ntok), n1 = ntok - kSub, n2 = ntok - 2 * kSub;
-                const uint32_t id0 = idesc_bf16(128, (n0 + 15) & ~15);
-                const uint32_t id1 = idesc_bf16(128, n1 <= 0 ? 16 : (min(kSub, n1) + 15) & ~15);
+                // tokens [0, 256) in one MMA of N <= 256 (columns 0..255), the rest
+                // (tokens 256..383) in a second one (columns 256..383): wide MMAs
+                // amortise the per-instruction cost of the A operand read from TMEM
+                const int nA = min(2 * kSub, (ntok + 15) & ~15);
+                const int n2 = ntok - 2 * kSub;
+                const uint32_t idA = idesc_bf16(128, nA);
                 const uint32_t id2 = idesc_bf16(128, n2 <= 0 ? 16 : (min(kSub, n2) + 15) & ~15);
                 // the epilogue of the previous tile must have drained the accumulators
                 if (!mbar_wait(&S.acc_empty, (it & 1) ^ 1, abort_flag, err)) break;
@@ -309,9 +201,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < kBK / 16; ++kk) {
                         const uint32_t a_t = tbase + kAcol + st * 32 + kk * 8;
                         const uint32_t acc = (kb | kk) != 0;
-                        mma_ts(tbase, a_t, smem_desc_sw128(bst + kk * 32), id0, acc);
-                        if (nsub > 1) mma_ts(tbase + kSub, a_t, smem_desc_sw128(bst + kSubBytes + kk * 32), id1, acc);
-                        if (nsub > 2) mma_ts(tbase + 2 * kSub, a_t, smem_desc_sw128(bst + 2 * kSubBytes + kk * 32), id2, acc);
+                        mma_ts(tbase, a_t, smem_desc_sw128(bst + kk * 32), idA, acc);
+                        if (n2 > 0) mma_ts(tbase + 2 * kSub, a_t, smem_desc_sw128(bst + 2 * kSubBytes + kk * 32), id2, acc);
                     }
                     mma_commit(&S.empty[st]);
                 }
@@ -327,6 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int hf = t >> 7;
         const uint32_t lane_off = ((uint32_t)(warp & 3) * 32) << 16;
         const int gs = w.group_size;
+        const int kpg = gs / kBK;                      // k-blocks per scale group
+        const bool kpg_pow2 = (kpg & (kpg - 1)) == 0;
+        const int kshift = __ffs(kpg) - 1;
         const unsigned short *s_ptr = reinterpret_cast<const unsigned short *>(w.s);
         const unsigned short *z_ptr = reinterpret_cast<const unsigned short *>(w.z);
         int g = 0, it = 0;
@@ -349,7 +243,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 crow = (int64_t)e * C + h0 + row;
             }
             const uint4 *qrow = reinterpret_cast<const uint4 *>((TRANS ? w.qT : w.qP) + crow * (K / 2)) + hf;
-            const int64_t gbase = crow * (int64_t)K;
+            // scale / zero group of k-block kb: groups run along K and hold gs / 64
+            // k-blocks, so it is g0 + kb / kpg (a shift when kpg is a power of two,
+            // as for group 128) -- no 64-bit division per k-block
+            const int64_t g0 = crow * (int64_t)(K / gs);
             // overlay queue of this lane: next two trained coordinates (K index, bf16 bits)
             const int32_t *ov_ptr = TRANS ? w.colT_ptr : w.row_ptr;
             const int32_t *ov_idx = TRANS ? w.rowT : w.col;
@@ -374,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     do {                                                                                         \
         A_ = __ldg(qrow + (kb_) * 2);                                                            \
         if (!TRANS) {                                                                            \
-            int64_t gg = (gbase + (int64_t)(kb_) * kBK) / gs;                                    \
+            const int64_t gg = g0 + (kpg_pow2 ? ((kb_) >> kshift) : ((kb_) / kpg));            \
             Z_.x = __ldg(s_ptr + gg);                                                            \
             Z_.y = __ldg(z_ptr + gg);                                                            \
         }                                                                                        \
@@ -453,7 +350,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             int j0 = 0, h0 = 0;
             if (MODE == MODE_GATE_UP) j0 = rb * 64;
             else h0 = rb * 128;
-            if (!mbar_wait(&S.acc, it & 1, abort_flag, err)) break;
+            // one decision for the 128 epilogue threads: the loop below syncs them on
+            // a named barrier, so none may leave it alone
+            if (!named_bar_and(2, 128, mbar_wait(&S.acc, it & 1, abort_flag, err))) break;
             tc_fence_after();
             const int gt = row;
             __nv_bfloat16 *stg_g = stg;

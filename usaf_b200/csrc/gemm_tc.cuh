@@ -15,4 +15,5 @@ int tc_down_bwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfl
                 const __nv_bfloat16 *gu, __nv_bfloat16 *dgu, cudaStream_t st);
 int tc_gate_up_bwd(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *dgu,
                    __nv_bfloat16 *dx_seg, cudaStream_t st);
+
 }  // namespace usaf

@@ -202,6 +202,20 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// named barrier that also ANDs a predicate over the participating threads:
+// every one of them gets the same answer (a decision all of them must take
+// together, e.g. whether to leave a loop that contains other named barriers)
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
 // named barrier for a subset of warps
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
