@@ -145,8 +145,8 @@ def test_sgd_router_step_bf16(dev, golden_dir):
     """train.py's SGD-momentum router step (train.py:494-498, 667-672) on the
     bf16 mini case, two steps: the router's bf16 momentum buffer within the
     dW_r tolerance, and W_r off the oracle's by no more than what the two
-    momentum buffers' difference moves it (lr * |buf_dev - buf_ref|) plus two
-    bf16 ulps of rounding."""
+    momentum buffers' difference moves it (lr * |buf_dev - buf_ref|) plus the
+    bf16 rounding of the weight and of the update."""
     import os
     g = torch.load(os.path.join(golden_dir, "bf16_mini.pt"), weights_only=False)
     inp = make_block_inputs(**MINI)
@@ -158,8 +158,13 @@ def test_sgd_router_step_bf16(dev, golden_dir):
         assert torch.equal(a["weights"] != 0, b["weights"] != 0), f"step {s}: routing differs"
         close(a["momentum"].float(), b["momentum"].float(), 2e-2, f"step {s} momentum")
         w_a, w_b = a["w_r_after"].float(), b["w_r_after"].float()
-        ulp = torch.finfo(torch.bfloat16).eps * torch.maximum(w_a.abs(), w_b.abs())
-        bound = lr * (a["momentum"].float() - b["momentum"].float()).abs() * (s + 1) + 2 * ulp + 1e-30
-        assert ((w_a - w_b).abs() <= bound).all(), f"step {s}: W_r off beyond the momentum difference"
+        ba, bb = a["momentum"].float(), b["momentum"].float()
+        # torch's CUDA SGD rounds w - lr * buf once, its CPU path may round the
+        # update first: two bf16 roundings of |w| + |lr * buf| per step
+        eps = torch.finfo(torch.bfloat16).eps
+        upd = lr * torch.maximum(ba.abs(), bb.abs())
+        bound = (lr * (ba - bb).abs() + 2 * eps * (torch.maximum(w_a.abs(), w_b.abs()) + upd)) * (s + 1)
+        bad = (w_a - w_b).abs() > bound
+        assert not bad.any(), f"step {s}: {int(bad.sum())} W_r entries off beyond the momentum difference"
         moved = (w_b != inp["w_r"].float()).float().mean().item()
         assert moved > 0.05, f"step {s}: the SGD step moved only {moved:.3f} of W_r"

@@ -61,8 +61,6 @@ class SparseMoELayer:
         steps the router with SparseAdam over all of W_r (the C2
         configuration); ``"sgd"`` with train.py's SGD, momentum 0.9 and the
         same weight decay (train.py:494-498, 667-672)."""
-        if router_optimizer not in ("adam", "sgd"):
-            raise ValueError(f"router_optimizer must be 'adam' or 'sgd', got {router_optimizer!r}")
         # compact vectors (masters, moments, gradients) in CSR order: the kernels'
         # compact <-> overlay maps become the identity (streaming accesses)
         self.active = {n: a.reshape(-1).long() for n, a in active.items()}
@@ -85,16 +83,23 @@ class SparseMoELayer:
         rname = self.prefix.replace(".experts", ".gate.weight")
         self.router_name = rname
         self.router_param = torch.nn.Parameter(self.w_r, requires_grad=False)
-        rlr = router_lr if router_lr is not None else lr
-        self.router_sgd = None
-        if router_optimizer == "sgd":
-            self.router_opt = None
-            self.router_sgd = torch.optim.SGD([self.router_param], lr=rlr, momentum=0.9,
+        self.use_router_optimizer(router_optimizer, router_lr if router_lr is not None else lr,
+                                  weight_decay)
+
+    def use_router_optimizer(self, kind: str, lr: float, weight_decay: float = 0.01):
+        """A fresh router optimizer: ``"adam"`` (SparseAdam over all of W_r) or
+        ``"sgd"`` (train.py's SGD, momentum 0.9, train.py:494-498)."""
+        if kind not in ("adam", "sgd"):
+            raise ValueError(f"router optimizer must be 'adam' or 'sgd', got {kind!r}")
+        E, H = self.w_r.shape
+        self.router_sgd = self.router_opt = None
+        if kind == "sgd":
+            self.router_sgd = torch.optim.SGD([self.router_param], lr=lr, momentum=0.9,
                                               weight_decay=weight_decay)
         else:
-            self.router_opt = SparseAdam({rname: self.router_param},
-                                         active_idx={rname: torch.arange(E * H, device=self.w_r.device)},
-                                         lr=rlr, weight_decay=weight_decay)
+            self.router_opt = SparseAdam({self.router_name: self.router_param},
+                                         active_idx={self.router_name: torch.arange(E * H, device=self.w_r.device)},
+                                         lr=lr, weight_decay=weight_decay)
 
     def train_step(self, x, dy, loss_scale: float = 1.0, accum: int = 1, micro=None):
         """One optimizer step over ``accum`` micro-batches (x, dy pairs)."""
