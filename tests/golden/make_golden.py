@@ -273,6 +273,51 @@ def run_rigl(ref_root):
     return out
 
 
+CLI_ARGS = [
+    ["--model", "Qwen/Qwen3-30B-A3B", "--dataset", "data/train.jsonl"],
+    ["--model", "m", "--dataset", "d.jsonl", "--steps", "360", "--epochs", "1.5", "--seq-len", "256",
+     "--microbatch", "4", "--accum", "8", "--frac", "0.01", "--lr", "1e-4", "--wd", "0.01",
+     "--train-from", "12", "--reselect-every", "25", "--no-frozen-cache", "--no-resident",
+     "--frozen-cache-n", "3", "--eval-every", "5", "--cuda", "--no-amp", "--no-multi-gpu", "--tag", "x",
+     "--checkpoint-dir", "ck", "--log-dir", "lg", "--resume", "r.pt", "--save-every", "10",
+     "--export", "e.pt", "--eval-only", "--eval-datasets", "a,b", "--eval-samples", "8",
+     "--eval-report", "rep.json"],
+    ["--model", "m", "--dataset", "d", "--no-cuda", "--quant-path", "q.pt"],
+]
+
+
+def cli_dataset_lines():
+    """A seeded JSONL: samples of 8 tokens, some of other lengths, a blank and
+    a malformed line (the loader skips those)."""
+    import json
+    import random as _r
+    rng = _r.Random(5)
+    lines = []
+    for i in range(46):
+        n = 8 if i % 7 else 6
+        lines.append(json.dumps({"input_ids": [rng.randrange(100) for _ in range(n)], "id": i}))
+    lines.insert(10, "")
+    lines.insert(20, "{not json")
+    return lines
+
+
+def run_cli(ref_root):
+    """The reference CLI's own parse_args on CLI_ARGS (usaf/train.py:131-171)
+    and its dataset loader (:173-194) on cli_dataset_lines()."""
+    import dataclasses
+    import tempfile
+    import usaf.train as ut
+    out = {"args": CLI_ARGS, "configs": [dataclasses.asdict(ut.parse_args(a)) for a in CLI_ARGS]}
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "data.jsonl")
+        with open(path, "w") as f:
+            f.write("\n".join(cli_dataset_lines()) + "\n")
+        tr, ev, he = ut._load_dataset(path, 8)
+    out["dataset"] = {"train": [s["id"] for s in tr], "eval": [s["id"] for s in ev],
+                      "heldout": [s["id"] for s in he]}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -293,6 +338,10 @@ def main():
         torch.save(run_ties(a.reference), os.path.join(HERE, "router_ties.pt"))
     if want("rigl"):
         torch.save(run_rigl(a.reference), os.path.join(HERE, "rigl.pt"))
+    if want("cli"):
+        import json
+        with open(os.path.join(HERE, "cli.json"), "w") as f:
+            json.dump(run_cli(a.reference), f, indent=1)
     print("golden fixtures written to", HERE)
 
 

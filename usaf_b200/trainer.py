@@ -108,13 +108,18 @@ class SparseTrainer:
     def __init__(self, model: torch.nn.Module, steps: int, lr_peak: float = 2e-4,
                  weight_decay: float = 0.005, accum: int = 1, frac: float = 0.005,
                  reselect_every: int = 50, loss_scale_init: float = LOSS_SCALE_INIT,
-                 scale_up_every: int = SCALE_UP_EVERY, train_router: bool = True):
+                 scale_up_every: int = SCALE_UP_EVERY, train_router: bool = True,
+                 expert_names: Optional[Iterable[str]] = None):
+        """``expert_names``: the ``*.mlp.experts`` modules to train (default:
+        every one with int4 weights attached); the others run frozen."""
         self.model = model
         self.steps, self.lr_peak, self.weight_decay = int(steps), float(lr_peak), float(weight_decay)
         self.accum, self.frac, self.reselect_every = int(accum), float(frac), int(reselect_every)
+        wanted = set(expert_names) if expert_names is not None else None
         self.experts: Dict[str, torch.nn.Module] = {
             n: m for n, m in model.named_modules()
-            if n.endswith(".mlp.experts") and getattr(m, "_usaf_int4", None) is not None}
+            if n.endswith(".mlp.experts") and getattr(m, "_usaf_int4", None) is not None
+            and (wanted is None or n in wanted)}
         if not self.experts:
             raise ValueError("no experts with int4 weights attached (attach_int4_experts)")
         self.projections: Dict[str, Projection] = {}
