@@ -195,6 +195,8 @@ def run_ours(args, rank, world, local_rank):
     else:
         layer, x, dy = build_layer(dev, 1 + rank)
         blk = layer.block
+    # the importance pass's dense |grad| buffers are gone: return their memory
+    torch.cuda.empty_cache()
     T = CFG["T"]
     # timed kernel: the grouped gate_up dequant GEMM (+SwiGLU) of the forward
     k_ev = []
