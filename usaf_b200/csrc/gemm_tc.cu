@@ -359,7 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c0 = 0; c0 < ntok; c0 += 32) {
                 // MODE_DOWN_BWD: this thread's forward gate/up vectors for the chunk
                 // (items gt + 128 q: token j = gt/16 + 8 q, column group gt%16), loaded
-                // before the TMEM drain so their latency overlaps it
+                // before the TMEM drain so their latency overlaps it (loading them a
+                // chunk earlier measured slower)
                 uint4 gpre[4], upre[4];
                 if (MODE == MODE_DOWN_BWD) {
 #pragma unroll
@@ -381,14 +382,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     stg_g[i * kStageLd + row] = __float2bfloat16_rn(__uint_as_float(v[i]));
                 named_bar_sync(1, 128);
                 if (MODE == MODE_DOWN || MODE == MODE_GU_BWD) {
+                    // four 16-byte items per thread: all loads first, then all stores
                     const int ld = MODE == MODE_DOWN ? R : C;
-                    for (int item = gt; item < 32 * 16; item += 128) {
-                        const int j = item >> 4, sg = item & 15;
-                        if (c0 + j < ntok) {
-                            const int64_t slot = row0 + c0 + j;
-                            *reinterpret_cast<uint4 *>(out0 + slot * ld + h0 + sg * 8) =
-                                *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
-                        }
+                    uint4 val[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int item = gt + 128 * q, j = item >> 4, sg = item & 15;
+                        val[q] = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int item = gt + 128 * q, j = item >> 4, sg = item & 15;
+                        if (c0 + j < ntok)
+                            *reinterpret_cast<uint4 *>(out0 + (int64_t)(row0 + c0 + j) * ld + h0 + sg * 8) = val[q];
                     }
                 } else if (MODE == MODE_GATE_UP) {
                     const int I = R / 2;
@@ -419,33 +425,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {  // MODE_DOWN_BWD: SwiGLU backward with the forward's gate/up
                     const int I = C;
+                    uint4 dv[4];
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const int j = (gt >> 4) + 8 * q, sg = gt & 15;
+                        dv[q] = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
+                    }
+                    const uint64_t one2 = f2_pack(1.0f, 1.0f);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int j = (gt >> 4) + 8 * q, sg = gt & 15;
+                        const uint32_t dw[4] = {dv[q].x, dv[q].y, dv[q].z, dv[q].w};
+                        const uint32_t gw[4] = {gpre[q].x, gpre[q].y, gpre[q].z, gpre[q].w};
+                        const uint32_t uw[4] = {upre[q].x, upre[q].y, upre[q].z, upre[q].w};
+                        // this item's slot takes the next chunk's vectors, in flight
+                        // during the rest of this chunk
+                        uint32_t dg4[4], du4[4];
+#pragma unroll
+                        for (int w2 = 0; w2 < 4; ++w2) {
+                            // two elements per packed fp32 operation; fast exp / reciprocal:
+                            // the backward products are rounded to bf16, a few fp32 ulps
+                            // do not survive that
+                            const uint64_t dh2 = bf2_to_f2(dw[w2]), g2 = bf2_to_f2(gw[w2]);
+                            const uint64_t u2 = bf2_to_f2(uw[w2]);
+                            const uint64_t den2 = f2_add(one2, f2_pack(__expf(-f2_lo(g2)), __expf(-f2_hi(g2))));
+                            const uint64_t sig2 = f2_pack(__fdividef(1.0f, f2_lo(den2)), __fdividef(1.0f, f2_hi(den2)));
+                            const uint64_t sgr2 = bf2_to_f2(f2_to_bf2(f2_mul(g2, sig2)));
+                            const uint64_t dsr2 = bf2_to_f2(f2_to_bf2(f2_mul(dh2, u2)));
+                            du4[w2] = f2_to_bf2(f2_mul(dh2, sgr2));
+                            const uint64_t tt2 = f2_add(one2, f2_mul(g2, f2_sub(one2, sig2)));
+                            dg4[w2] = f2_to_bf2(f2_mul(f2_mul(dsr2, sig2), tt2));
+                        }
                         if (c0 + j < ntok) {
                             const int64_t slot = row0 + c0 + j;
                             const int i0 = h0 + sg * 8;
-                            const uint4 dv = *reinterpret_cast<const uint4 *>(stg_g + j * kStageLd + sg * 8);
-                            const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
-                            const uint32_t gw[4] = {gpre[q].x, gpre[q].y, gpre[q].z, gpre[q].w};
-                            const uint32_t uw[4] = {upre[q].x, upre[q].y, upre[q].z, upre[q].w};
-                            uint32_t dg4[4], du4[4];
-                            const uint64_t one2 = f2_pack(1.0f, 1.0f);
-#pragma unroll
-                            for (int w2 = 0; w2 < 4; ++w2) {
-                                // two elements per packed fp32 operation; fast exp / reciprocal:
-                                // the backward products are rounded to bf16, a few fp32 ulps
-                                // do not survive that
-                                const uint64_t dh2 = bf2_to_f2(dw[w2]), g2 = bf2_to_f2(gw[w2]);
-                                const uint64_t u2 = bf2_to_f2(uw[w2]);
-                                const uint64_t den2 = f2_add(one2, f2_pack(__expf(-f2_lo(g2)), __expf(-f2_hi(g2))));
-                                const uint64_t sig2 = f2_pack(__fdividef(1.0f, f2_lo(den2)), __fdividef(1.0f, f2_hi(den2)));
-                                const uint64_t sgr2 = bf2_to_f2(f2_to_bf2(f2_mul(g2, sig2)));
-                                const uint64_t dsr2 = bf2_to_f2(f2_to_bf2(f2_mul(dh2, u2)));
-                                du4[w2] = f2_to_bf2(f2_mul(dh2, sgr2));
-                                const uint64_t tt2 = f2_add(one2, f2_mul(g2, f2_sub(one2, sig2)));
-                                dg4[w2] = f2_to_bf2(f2_mul(f2_mul(dsr2, sig2), tt2));
-                            }
                             *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + i0) = make_uint4(dg4[0], dg4[1], dg4[2], dg4[3]);
                             *reinterpret_cast<uint4 *>(out0 + slot * 2 * I + I + i0) = make_uint4(du4[0], du4[1], du4[2], du4[3]);
                         }
