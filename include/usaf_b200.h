@@ -90,6 +90,12 @@ typedef struct {
      * is set for every overlay coordinate (e, r, c).  Optional (NULL selects
      * the SIMT gradient kernel); the tensor-core usaf_sparse_dw reads it. */
     const uint32_t *ov_mask;
+    /* overlay positions per 256-column block [E*R*ceil(C/256)*2]: entry
+     * ((e*R + r)*ceil(C/256) + b)*2 + h is the CSR position of the first entry
+     * of segment (row e*R + r, half h) whose column is >= 256*b
+     * (usaf_build_ov_cbptr).  The tensor-core usaf_sparse_dw needs it with
+     * ov_mask; NULL selects the SIMT gradient kernel. */
+    const int32_t *ov_cbptr;
 } usaf_qweight;
 
 /* ---- int4 format ---------------------------------------------------------
@@ -291,6 +297,11 @@ int usaf_dot(const void *a, const void *b, int32_t dtype, int64_t n, float *out,
  * row keys (n_rows + 1 entries). */
 int usaf_build_rowptr(const int64_t *keys, int64_t n, int64_t n_rows, int32_t *row_ptr,
                       void *stream);
+/* usaf_build_ov_cbptr: usaf_qweight.ov_cbptr from the overlay's CSR
+ * (row_ptr [E*R*2+1], col [n_ov]) of a projection [E, R, C]; out holds
+ * E*R*ceil(C/256)*2 int32. */
+int usaf_build_ov_cbptr(const int32_t *row_ptr, const int32_t *col, int32_t E, int32_t R, int32_t C,
+                        int32_t *out, void *stream);
 const char *usaf_version(void);
 
 /* ---- expert parallelism ------------------------------------------------------

@@ -33,7 +33,7 @@ class QWeight(C.Structure):
                 ("q", P), ("s", P), ("z", P), ("n_ov", I32),
                 ("row_ptr", P), ("col", P), ("val", P),
                 ("colT_ptr", P), ("rowT", P), ("valT", P), ("qT", P), ("szT", P), ("qP", P),
-                ("ov_mask", P)]
+                ("ov_mask", P), ("ov_cbptr", P)]
 
 
 # name -> (restype, argtypes)
@@ -68,6 +68,7 @@ _SIGS = {
     "usaf_sort_u32": (I32, [P, P, I64, P, P, I32, P, P]),
     "usaf_dot": (I32, [P, P, I32, I64, P, P]),
     "usaf_build_rowptr": (I32, [P, I64, I64, P, P]),
+    "usaf_build_ov_cbptr": (I32, [P, P, I32, I32, I32, P, P]),
     "usaf_version": (C.c_char_p, []),
 }
 

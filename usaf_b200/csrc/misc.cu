@@ -1,7 +1,8 @@
 // Small utilities of the C ABI: a deterministic dot product (the step's
 // scalar readback; its block partials live in a fixed array of this library,
 // so two dot products in flight at once on one device race), CSR row pointers
-// from sorted row keys, and the version.
+// from sorted row keys, the overlay's per-column-block positions, and the
+// version.
 #include "common.cuh"
 
 namespace usaf {
@@ -65,6 +66,22 @@ __global__ void rowptr_kernel(const int64_t *__restrict__ keys, int64_t n, int64
     }
 }
 
+// one thread per CSR segment (row, half): the first position of each
+// 256-column block inside the segment (columns ascend within a segment)
+__global__ void ov_cbptr_kernel(const int32_t *__restrict__ row_ptr, const int32_t *__restrict__ col,
+                                int64_t n_seg, int ncb, int32_t *__restrict__ out) {
+    for (int64_t sg = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; sg < n_seg;
+         sg += (int64_t)gridDim.x * blockDim.x) {
+        int p = row_ptr[sg];
+        const int end = row_ptr[sg + 1];
+        const int64_t row = sg >> 1, h = sg & 1;
+        for (int b = 0; b < ncb; ++b) {
+            while (p < end && col[p] < 256 * b) ++p;
+            out[(row * ncb + b) * 2 + h] = p;
+        }
+    }
+}
+
 }  // namespace usaf
 
 using namespace usaf;
@@ -90,6 +107,18 @@ extern "C" int usaf_build_rowptr(const int64_t *keys, int64_t n, int64_t n_rows,
     cudaStream_t st = as_stream(stream);
     unsigned grid = (unsigned)std::min<int64_t>((n_rows + 256) / 256, 148 * 8);
     rowptr_kernel<<<grid, 256, 0, st>>>(keys, n, n_rows, row_ptr);
+    USAF_CHECK_LAUNCH();
+    return USAF_OK;
+}
+
+extern "C" int usaf_build_ov_cbptr(const int32_t *row_ptr, const int32_t *col, int32_t E, int32_t R,
+                                   int32_t C, int32_t *out, void *stream) {
+    USAF_REQUIRE(row_ptr && out && E >= 0 && R >= 0 && C >= 1);
+    const int64_t n_seg = (int64_t)E * R * 2;
+    if (n_seg == 0) return USAF_OK;
+    cudaStream_t st = as_stream(stream);
+    unsigned grid = (unsigned)std::min<int64_t>((n_seg + 255) / 256, 148 * 8);
+    ov_cbptr_kernel<<<grid, 256, 0, st>>>(row_ptr, col, n_seg, (C + 255) / 256, out);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }

@@ -8,24 +8,41 @@
 // D_e is formed tile by tile in TMEM and never written out: the epilogue
 // keeps what the caller needs.
 //   EPI_SPARSE   : the selected coordinates, read from the overlay bitmap, as
-//                  dtype(D) into a CSR-ordered fp32 vector; a second kernel
-//                  adds scale * that value to the compact gradient.
+//                  dtype(D) into a CSR-ordered fp32 vector (stores only: a
+//                  read-modify-write of the compact vector here would wait on
+//                  each scattered load in turn); a second kernel adds
+//                  scale * that value to the compact vector.
 //   EPI_DENSE_ABS: |dtype(D)| at every coordinate (importance pass,
 //                  usaf/importance.py).
 //
-// Tile = 128 storage rows x 256 columns, K = the expert's slots in blocks of
-// 64.  Both operands reach shared memory as TMA boxes of 64 slots x 64
-// rows/columns with the 128-byte swizzle; for the MMA they are MN-major
-// (rows r / columns c contiguous, slots along K), so no transpose is needed.
-// Slots of the next expert that fall inside the last 16-slot group the MMA
-// reads are zeroed in shared memory before it does.
+// Tile = 128 storage rows x 256 columns (MMA M x N), K = the expert's slots in
+// blocks of 64.  Both operands reach shared memory as TMA boxes of 64 slots x
+// 64 rows/columns with the 128-byte swizzle, MN-major for the MMA (rows r /
+// columns c contiguous, slots along K), so no transpose is needed.
 //
-// Persistent CTAs (one per SM) walk work items (expert, 128-row block); an
-// item runs its column tiles back to back.  Warp 0 issues TMA, warp 1 the
-// MMAs (and owns TMEM), warps 2-5 drain the accumulators, warp 6 passes each
-// filled stage on to the MMA after zeroing the ragged tail of an expert's
-// last k-block; TMEM holds two 256-column
-// accumulators so the drain of one tile overlaps the MMAs of the next.
+// Work order: the tiles are numbered column-block-major, then expert, then
+// row block, and every CTA (one per SM, persistent) takes one contiguous
+// range of them, cut so that the ranges cost the same (a tile's cost grows
+// with its expert's slot count).  Inside a range, a run of row blocks of one
+// (expert, column block) keeps the gin block -- 256 columns x up to 320
+// slots -- resident in shared memory and streams only the 128-row gout
+// blocks, so the operand traffic per tile is about a third of loading both.
+// (Expert-major numbering measured slower: each CTA then streams one
+// expert's gout once per column block, and 148 of those no longer fit in L2;
+// processing the experts in waves of 32 measured the same as this order.)
+// Experts with more slots run in chunks of at most 320 slots; the partial
+// sums of a chunk go through fp32 in the output vector and are rounded after
+// the last chunk.
+//
+// Warp 0 issues TMA; warp 18 forwards every filled stage to the MMA after
+// zeroing the slots past an expert's end inside its last 16-slot group (they
+// belong to the next expert), so the MMA issuer -- lane 0 of warp 1, which
+// also owns TMEM -- runs a lean loop of waits, MMAs and commits (its own
+// per-k-block bookkeeping otherwise outlasts the four MMAs it issues); warps
+// 2-17 drain the accumulators, four per TMEM lane quarter (64 columns each),
+// so every scheduler has four drain warps to interleave.  TMEM holds two
+// 256-column accumulators, so the drain of one tile overlaps the MMAs of the
+// next.
 #include <cudaTypedefs.h>
 
 #include "tc_common.cuh"
@@ -38,27 +55,37 @@ namespace {
 constexpr int kSM = 128;                 // storage rows per tile (MMA M)
 constexpr int kSN = 256;                 // columns per tile (MMA N)
 constexpr int kSK = 64;                  // slots per k-block
-constexpr int kSStages = 4;
-constexpr int kSThreads = 224;
+constexpr int kAStages = 4;              // gout ring
+constexpr int kBMaxKb = 5;               // resident gin k-blocks (320 slots)
+constexpr int kSThreads = 608;           // 19 warps
+constexpr int kEpiThreads = 512;         // warps 2-17
+constexpr int kFwdWarp = 18;             // the stage forwarder
 constexpr int kBox = kSK * 64 * 2;       // one TMA box: 64 slots x 64 bf16 = 8 KB
 constexpr int kAStage = 2 * kBox;        // 128 rows
-constexpr int kStage = kAStage + 4 * kBox;   // + 256 columns = 48 KB
-constexpr int kRowLd = 33;               // epilogue per-thread row (floats)
+constexpr int kBKb = 4 * kBox;           // 256 columns
+constexpr uint32_t kFull = 0xffffffffu;
 
 enum : int { EPI_SPARSE = 0, EPI_DENSE_ABS = 1 };
+// how a tile's sums combine with the other slot chunks of its expert
+enum : int { PART_ALL = 0, PART_FIRST = 1, PART_MID = 2, PART_LAST = 3 };
 
 struct alignas(8) SShared {
-    uint64_t full[kSStages];
-    uint64_t empty[kSStages];
+    uint64_t a_full[kAStages];
+    uint64_t a_empty[kAStages];
+    uint64_t a_ready[kAStages];
+    uint64_t b_full[kBMaxKb];
+    uint64_t b_ready[kBMaxKb];
+    uint64_t b_empty;
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
-    uint64_t fixed[kSStages];
     uint64_t mma_done;
     uint32_t tmem_base;
     int abort_flag;
+    int t_lo, t_hi;                          // this CTA's tile range
 };
 
-constexpr size_t kSSmem = (size_t)kSStages * kStage + (size_t)128 * kRowLd * 4 + sizeof(SShared) + 1024;
+constexpr size_t kSSmem = (size_t)kAStages * kAStage + (size_t)kBMaxKb * kBKb + sizeof(SShared) + 1024;
+static_assert(kSSmem <= 232448, "SDDMM shared memory above the per-block limit");
 
 __device__ __forceinline__ void s_drain(uint64_t *bar, uint32_t parity, int *err) {
     uint64_t t0 = globaltimer();
@@ -96,111 +123,340 @@ __device__ __forceinline__ float round_bf16(float v) {
     return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// ---- work order ----------------------------------------------------------------
+
+// cost of one tile of an expert with `cnt` slots, in units of one 16-slot MMA
+// step (the fixed part stands for the epilogue and the stream of gout)
+__device__ __forceinline__ int64_t tile_cost(int cnt, int dense) {
+    if (cnt <= 0) return dense ? 40 : 2;
+    return (cnt + 15) / 16 + (dense ? 40 : 6);
+}
+
+// tiles of one (column block, expert) run (nrb of them, `wt` each, the first
+// at cost prefix `cum`) whose cost prefix lies below x
+__device__ __forceinline__ int64_t tiles_below(int64_t x, int64_t cum, int64_t wt, int nrb) {
+    if (x <= cum) return 0;
+    if (wt == 0) return nrb;
+    return min((int64_t)nrb, (x - cum + wt - 1) / wt);
+}
+
+__device__ __forceinline__ int64_t warp_sum64(int64_t v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+// one warp: this CTA's tile range [t_lo, t_hi) -- the tiles whose cost prefix
+// falls in the CTA's equal share of the total
+__device__ void tile_range(const usaf_route_plan &pl, int nrb, int ncb, int dense, int lane, int *t_lo,
+                           int *t_hi) {
+    const int E = pl.E;
+    int64_t We = 0;   // cost of one column block over all experts
+    for (int e0 = 0; e0 < E; e0 += 32) {
+        const int e = e0 + lane;
+        We += e < E ? tile_cost(__ldg(pl.expert_cnt + e), dense) * nrb : 0;
+    }
+    We = warp_sum64(We);
+    const int64_t W = We * ncb, G = gridDim.x, b = blockIdx.x;
+    const int64_t x0 = W * b / G, x1 = W * (b + 1) / G;
+    int64_t n0 = 0, n1 = 0;
+    for (int cb = 0; cb < ncb; ++cb) {
+        int64_t carry = We * cb;
+        if (carry >= x1) break;   // this column block and the later ones lie above both bounds
+        if (carry + We <= x0) {   // the whole column block lies below both bounds
+            if (lane == 0) {
+                n0 += (int64_t)E * nrb;
+                n1 += (int64_t)E * nrb;
+            }
+            continue;
+        }
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const int64_t wt = e < E ? tile_cost(__ldg(pl.expert_cnt + e), dense) : 0;
+            const int64_t w = wt * nrb;
+            int64_t incl = w;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int64_t y = __shfl_up_sync(kFull, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const int64_t cum = carry + incl - w;
+            carry += __shfl_sync(kFull, incl, 31);
+            if (e < E) {
+                n0 += tiles_below(x0, cum, wt, nrb);
+                n1 += tiles_below(x1, cum, wt, nrb);
+            }
+        }
+    }
+    n0 = warp_sum64(n0);
+    n1 = warp_sum64(n1);
+    *t_lo = (int)n0;
+    *t_hi = b == G - 1 ? E * nrb * ncb : (int)n1;
+}
+
+// a run of row blocks [rb0, rb1) of one (column block, expert) inside [t, t_hi)
+struct Run {
+    int e, cb, rb0, rb1;
+};
+
+__device__ __forceinline__ Run run_at(int t, int t_hi, int nrb, int E) {
+    Run s;
+    const int per_cb = nrb * E;
+    s.cb = t / per_cb;
+    const int r = t - s.cb * per_cb;
+    s.e = r / nrb;
+    s.rb0 = r - s.e * nrb;
+    s.rb1 = min(nrb, s.rb0 + (t_hi - t));
+    return s;
+}
+
+// an expert's k-blocks in slot chunks of at most kBMaxKb k-blocks
+struct Chunks {
+    int nk, n, per;
+};
+
+__device__ __forceinline__ Chunks chunks_of(int cnt) {
+    Chunks c;
+    c.nk = (cnt + kSK - 1) / kSK;
+    c.n = (c.nk + kBMaxKb - 1) / kBMaxKb;
+    c.per = c.n ? (c.nk + c.n - 1) / c.n : 0;
+    return c;
+}
+
+// ---- MMA-side helpers ----------------------------------------------------------
+
+// all lanes of the warp wait; the answer is the same for every lane
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *err) {
+    return __all_sync(kFull, mbar_wait(bar, parity, abort_flag, err));
+}
+
+// zero slot rows [rem, round16(rem)) of `nbox` consecutive 64-slot boxes: a
+// full 128-byte slot row holds exactly that slot's 64 elements under the
+// 128-byte swizzle, whatever their order inside the row
+__device__ __forceinline__ void zero_tail(unsigned char *base, int nbox, int rem, int lane) {
+    const int per_box = (((rem + 15) & ~15) - rem) * 8;   // 16-byte chunks per box
+    for (int i = lane; i < nbox * per_box; i += 32) {
+        const int bx = i / per_box, k = i - bx * per_box;
+        *reinterpret_cast<uint4 *>(base + bx * kBox + rem * 128 + k * 16) = make_uint4(0, 0, 0, 0);
+    }
+}
+
+// ---- epilogue helpers ------------------------------------------------------------
+
+// global store that does not allocate a line in L1: the drain's stores are
+// scattered 4-byte writes nothing on this SM reads again (allocating them
+// measured ~25 % slower)
+__device__ __forceinline__ void st_na(float *p, float v) {
+    asm volatile("st.global.L1::no_allocate.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void emit_sparse(float *__restrict__ out, int mode, int p, float v) {
+    if (mode == PART_MID || mode == PART_LAST) v = __fadd_rn(out[p], v);
+    st_na(out + p, (mode == PART_ALL || mode == PART_LAST) ? round_bf16(v) : v);
+}
+
+// the selected columns of one 32-column chunk of this thread's row (values v,
+// bitmap word m), in ascending column order from CSR position p on: one
+// predicated store per column, straight-line code without a dependence from
+// one column to the next but the position counter
+__device__ __forceinline__ void drain_sparse(const uint32_t (&v)[32], uint32_t m, int &p, int mode,
+                                             float *__restrict__ out) {
+    if (mode == PART_ALL) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (m & (1u << i)) st_na(out + p++, round_bf16(__uint_as_float(v[i])));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (m & (1u << i)) emit_sparse(out, mode, p++, __uint_as_float(v[i]));
+    }
+}
+
+// bitmap words of chunks 2 slice and 2 slice + 1 of the row's column block
+// (w.x even chunk, w.y odd chunk) and the CSR positions where they start in
+// the row's two halves (p0 even chunks, p1 odd chunks): the block's start
+// positions plus the selected entries of the block's earlier chunks
+__device__ __forceinline__ void slice_start(const uint32_t *__restrict__ mask, const int32_t *__restrict__ cbptr,
+                                            int64_t grow, int C, int ncb, int cb, int slice, uint2 &w, int &p0,
+                                            int &p1) {
+    const uint32_t *mrow = mask + grow * (C / 32) + cb * 8;
+    const uint4 mlo = __ldg(reinterpret_cast<const uint4 *>(mrow));
+    const uint4 mhi = slice >= 2 ? __ldg(reinterpret_cast<const uint4 *>(mrow) + 1) : make_uint4(0, 0, 0, 0);
+    const int2 pp = __ldg(reinterpret_cast<const int2 *>(cbptr + (grow * ncb + cb) * 2));
+    int b0 = 0, b1 = 0;
+    if (slice >= 1) { b0 += __popc(mlo.x); b1 += __popc(mlo.y); }
+    if (slice >= 2) { b0 += __popc(mlo.z); b1 += __popc(mlo.w); }
+    if (slice >= 3) { b0 += __popc(mhi.x); b1 += __popc(mhi.y); }
+    w = slice == 0 ? make_uint2(mlo.x, mlo.y) : slice == 1 ? make_uint2(mlo.z, mlo.w)
+      : slice == 2 ? make_uint2(mhi.x, mhi.y) : make_uint2(mhi.z, mhi.w);
+    p0 = pp.x + b0;
+    p1 = pp.y + b1;
+}
+
+__device__ __forceinline__ void drain_dense(const uint32_t (&v)[32], float *o, int mode) {
+    float4 *o4 = reinterpret_cast<float4 *>(o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float4 a = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+        if (mode == PART_MID || mode == PART_LAST) {
+            const float4 b = o4[i];
+            a = make_float4(__fadd_rn(b.x, a.x), __fadd_rn(b.y, a.y), __fadd_rn(b.z, a.z), __fadd_rn(b.w, a.w));
+        }
+        if (mode == PART_ALL || mode == PART_LAST)
+            a = make_float4(fabsf(round_bf16(a.x)), fabsf(round_bf16(a.y)), fabsf(round_bf16(a.z)),
+                            fabsf(round_bf16(a.w)));
+        o4[i] = a;
+    }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kSThreads, 1)
     sddmm_tc_kernel(const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_in,
-                    usaf_route_plan pl, int R, int C, const int32_t *__restrict__ row_ptr,
-                    const uint32_t *__restrict__ mask, float *__restrict__ out) {
+                    usaf_route_plan pl, int R, int C, const uint32_t *__restrict__ mask,
+                    const int32_t *__restrict__ cbptr, float *__restrict__ out) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *sb = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    float *rows_s = reinterpret_cast<float *>(sb + (size_t)kSStages * kStage);
-    SShared &S = *reinterpret_cast<SShared *>(sb + (size_t)kSStages * kStage + (size_t)128 * kRowLd * 4);
+    unsigned char *a_ring = sb;
+    unsigned char *b_res = sb + (size_t)kAStages * kAStage;
+    SShared &S = *reinterpret_cast<SShared *>(b_res + (size_t)kBMaxKb * kBKb);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int E = pl.E;
     const int nrb = R / kSM;
     const int ncb = (C + kSN - 1) / kSN;
-    const int n_items = E * nrb;
     int *err = pl.err;
-    if (tid == 0) {
-        S.abort_flag = 0;
-        for (int s = 0; s < kSStages; ++s) {
-            mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], 1);
-            mbar_init(&S.fixed[s], 1);
+    if (warp == 0) {
+        if (lane == 0) {
+            S.abort_flag = 0;
+            for (int s = 0; s < kAStages; ++s) {
+                mbar_init(&S.a_full[s], 1);
+                mbar_init(&S.a_empty[s], 1);
+                mbar_init(&S.a_ready[s], 1);
+            }
+            for (int k = 0; k < kBMaxKb; ++k) {
+                mbar_init(&S.b_full[k], 1);
+                mbar_init(&S.b_ready[k], 1);
+            }
+            mbar_init(&S.b_empty, 1);
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&S.acc_full[b], 1);
+                mbar_init(&S.acc_empty[b], kEpiThreads);
+            }
+            mbar_init(&S.mma_done, 1);
+            fence_barrier_init();
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&S.acc_full[b], 1);
-            mbar_init(&S.acc_empty[b], 128);
+        int lo, hi;
+        tile_range(pl, nrb, ncb, EPI == EPI_DENSE_ABS, lane, &lo, &hi);
+        if (lane == 0) {
+            S.t_lo = lo;
+            S.t_hi = hi;
         }
-        mbar_init(&S.mma_done, 1);
-        fence_barrier_init();
+    } else if (warp == 1) {
+        tmem_alloc(&S.tmem_base, 512);
     }
     __syncthreads();
-    volatile int *abort_flag = &S.abort_flag;
-    if (warp == 1) tmem_alloc(&S.tmem_base, 512);
-    __syncthreads();
     tc_fence_after();
+    volatile int *abort_flag = &S.abort_flag;
     const uint32_t tbase = S.tmem_base;
+    const int t_lo = S.t_lo, t_hi = S.t_hi;
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             prefetch_tmap(&tm_out);
             prefetch_tmap(&tm_in);
-            int g = 0, last_g = -1;
-            for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
-                const int e = item / nrb, rb = item % nrb;
-                const int cnt = pl.expert_cnt[e];
-                if (cnt == 0) continue;
-                const int row0 = pl.expert_off[e];
-                const int nk = (cnt + kSK - 1) / kSK;
-                bool ok = true;
-                for (int cb = 0; cb < ncb && ok; ++cb) {
-                    const int c0 = cb * kSN;
-                    const int nb = min(4, (C - c0) / 64);
-                    for (int kb = 0; kb < nk; ++kb, ++g) {
-                        const int st = g % kSStages;
-                        if (!mbar_wait(&S.empty[st], ((g / kSStages) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
-                        mbar_arrive_expect_tx(&S.full[st], (uint32_t)((2 + nb) * kBox));
-                        unsigned char *dst = sb + (size_t)st * kStage;
-                        const int y = row0 + kb * kSK;
-                        tma_load_2d(dst, &tm_out, &S.full[st], rb * kSM, y);
-                        tma_load_2d(dst + kBox, &tm_out, &S.full[st], rb * kSM + 64, y);
-                        for (int j = 0; j < nb; ++j)
-                            tma_load_2d(dst + kAStage + j * kBox, &tm_in, &S.full[st], c0 + 64 * j, y);
-                        last_g = g;
+            int ga = 0, bc = 0;
+            bool ok = true;
+            for (int t = t_lo; t < t_hi && ok;) {
+                const Run s = run_at(t, t_hi, nrb, pl.E);
+                t += s.rb1 - s.rb0;
+                const int cnt = pl.expert_cnt[s.e];
+                const int row0 = pl.expert_off[s.e];
+                const Chunks ch = chunks_of(cnt);
+                const int c0 = s.cb * kSN;
+                const int nb = min(4, (C - c0) / 64);
+                for (int kc = 0; kc < ch.n && ok; ++kc) {
+                    const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
+                    // the previous chunk's MMAs have read the resident block
+                    if (!mbar_wait(&S.b_empty, (bc & 1) ^ 1, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    // every b_full barrier completes once per chunk (unused ones by a
+                    // plain arrive), so their phases stay in step with the chunk count
+                    for (int k = 0; k < kBMaxKb; ++k) {
+                        if (k < kb1 - kb0) {
+                            mbar_arrive_expect_tx(&S.b_full[k], (uint32_t)(nb * kBox));
+                            const int y = row0 + (kb0 + k) * kSK;
+                            for (int j = 0; j < nb; ++j)
+                                tma_load_2d(b_res + (size_t)k * kBKb + j * kBox, &tm_in, &S.b_full[k], c0 + 64 * j, y);
+                        } else {
+                            mbar_arrive(&S.b_full[k]);
+                        }
+                    }
+                    ++bc;
+                    for (int rb = s.rb0; rb < s.rb1 && ok; ++rb) {
+                        for (int kb = kb0; kb < kb1; ++kb, ++ga) {
+                            const int st = ga % kAStages;
+                            if (!mbar_wait(&S.a_empty[st], ((ga / kAStages) & 1) ^ 1, abort_flag, err)) {
+                                ok = false;
+                                break;
+                            }
+                            mbar_arrive_expect_tx(&S.a_full[st], (uint32_t)(2 * kBox));
+                            unsigned char *dst = a_ring + (size_t)st * kAStage;
+                            const int y = row0 + kb * kSK;
+                            tma_load_2d(dst, &tm_out, &S.a_full[st], rb * kSM, y);
+                            tma_load_2d(dst + kBox, &tm_out, &S.a_full[st], rb * kSM + 64, y);
+                        }
                     }
                 }
-                if (!ok) break;
             }
-            if (*abort_flag)
-                for (int gg = max(0, last_g - kSStages + 1); gg <= last_g; ++gg)
-                    s_drain(&S.full[gg % kSStages], (gg / kSStages) & 1, err);
+            if (*abort_flag) {
+                // loads in flight land before the CTA's shared memory is released
+                for (int g = max(0, ga - kAStages); g < ga; ++g)
+                    s_drain(&S.a_full[g % kAStages], (g / kAStages) & 1, err);
+                if (bc > 0)
+                    for (int k = 0; k < kBMaxKb; ++k) s_drain(&S.b_full[k], (bc - 1) & 1, err);
+            }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- MMA issuer (lane 0) ----------------
         if (lane == 0) {
-            int g = 0, it = 0;
+            const uint32_t a_s0 = smem_u32(a_ring), b_s0 = smem_u32(b_res);
+            int ga = 0, bc = 0, it = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-                const int e = item / nrb;
-                const int cnt = pl.expert_cnt[e];
-                if (cnt == 0) continue;
-                const int nk = (cnt + kSK - 1) / kSK;
-                for (int cb = 0; cb < ncb && ok; ++cb, ++it) {
-                    const int c0 = cb * kSN;
-                    const int nb = min(4, (C - c0) / 64);
-                    const uint32_t idesc = idesc_mn(kSM, nb * 64);
-                    const int buf = it & 1;
-                    if (!mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err)) { ok = false; break; }
-                    tc_fence_after();
-                    for (int kb = 0; kb < nk; ++kb, ++g) {
-                        const int st = g % kSStages;
-                        const int rem = min(kSK, cnt - kb * kSK);
-                        // stages reach the MMA through the fixer warp (fixed[st] completes
-                        // once per fill, after any ragged-tail zeroing)
-                        if (!mbar_wait(&S.fixed[st], (g / kSStages) & 1, abort_flag, err)) { ok = false; break; }
+            for (int t = t_lo; t < t_hi && ok;) {
+                const Run s = run_at(t, t_hi, nrb, pl.E);
+                t += s.rb1 - s.rb0;
+                const int cnt = pl.expert_cnt[s.e];
+                const Chunks ch = chunks_of(cnt);
+                const int nb = min(4, (C - s.cb * kSN) / 64);
+                const uint32_t idesc = idesc_mn(kSM, nb * 64);
+                for (int kc = 0; kc < ch.n && ok; ++kc) {
+                    const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
+                    for (int rb = s.rb0; rb < s.rb1 && ok; ++rb, ++it) {
+                        const int buf = it & 1;
+                        if (!(ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err))) break;
                         tc_fence_after();
-                        const uint32_t a_s = smem_u32(sb + (size_t)st * kStage), b_s = a_s + kAStage;
-                        const int nks = (rem + 15) / 16;
-                        for (int kk = 0; kk < nks; ++kk)
-                            mma_ss(tbase + buf * kSN, desc_mn_sw128(a_s + kk * 2048),
-                                   desc_mn_sw128(b_s + kk * 2048), idesc, (kb | kk) != 0);
-                        mma_commit(&S.empty[st]);
+                        for (int kb = kb0; kb < kb1; ++kb, ++ga) {
+                            const int kbl = kb - kb0, st = ga % kAStages;
+                            // first tile of the chunk: the resident block is in place
+                            if (rb == s.rb0 && !(ok = mbar_wait(&S.b_ready[kbl], bc & 1, abort_flag, err))) break;
+                            if (!(ok = mbar_wait(&S.a_ready[st], (ga / kAStages) & 1, abort_flag, err))) break;
+                            tc_fence_after();
+                            const int nks = (min(kSK, cnt - kb * kSK) + 15) / 16;
+                            const uint32_t as = a_s0 + st * kAStage, bs = b_s0 + kbl * kBKb;
+                            for (int kk = 0; kk < nks; ++kk)
+                                mma_ss(tbase + buf * kSN, desc_mn_sw128(as + kk * 2048),
+                                       desc_mn_sw128(bs + kk * 2048), idesc, (kb > kb0 || kk > 0));
+                            mma_commit(&S.a_empty[st]);
+                        }
+                        if (!ok) break;
+                        mma_commit(&S.acc_full[buf]);
                     }
                     if (!ok) break;
-                    mma_commit(&S.acc_full[buf]);
+                    mma_commit(&S.b_empty);
+                    ++bc;
                 }
             }
             // every MMA this CTA issued has completed before TMEM is released
@@ -208,170 +464,131 @@ __global__ void __launch_bounds__(kSThreads, 1)
             s_drain(&S.mma_done, 0, err);
         }
         __syncwarp();
-    } else if (warp == 6) {
-        // ---------------- fixer: forwards every filled stage to the MMA ----------------
-        // Slots past the expert's end inside the last 16-slot group of its last
-        // k-block belong to the next expert (or lie past the routed slots).  The
-        // MMA reads whole 16-slot groups, so those rows are zeroed in every box
-        // of the stage first.  Forwarding every fill (not only ragged ones) keeps
-        // this warp in step with the stage phases.
-        int g = 0;
+    } else if (warp == kFwdWarp) {
+        // ---------------- forwarder: filled stage -> MMA, tails zeroed ----------------
+        int ga = 0, bc = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-            const int e = item / nrb;
-            const int cnt = pl.expert_cnt[e];
-            if (cnt == 0) continue;
-            const int nk = (cnt + kSK - 1) / kSK;
-            const int rem = cnt - (nk - 1) * kSK;
-            for (int cb = 0; cb < ncb && ok; ++cb) {
-                const int nb = min(4, (C - cb * kSN) / 64);
-                for (int kb = 0; kb < nk; ++kb, ++g) {
-                    const int st = g % kSStages;
-                    const uint32_t par = (g / kSStages) & 1;
-                    if (kb == nk - 1 && (rem % 16)) {
-                        ok = mbar_wait(&S.full[st], par, abort_flag, err);
-                        ok = __all_sync(0xffffffffu, ok);
-                        if (!ok) break;
-                        const int r1 = (rem + 15) & ~15;
-                        const int per_box = (r1 - rem) * 8;       // 16-byte chunks
-                        unsigned char *stage = sb + (size_t)st * kStage;
-                        for (int i = lane; i < (2 + nb) * per_box; i += 32) {
-                            const int bx = i / per_box, k = i % per_box;
-                            *reinterpret_cast<uint4 *>(stage + bx * kBox + rem * 128 + k * 16) =
-                                make_uint4(0, 0, 0, 0);
+        for (int t = t_lo; t < t_hi && ok;) {
+            const Run s = run_at(t, t_hi, nrb, pl.E);
+            t += s.rb1 - s.rb0;
+            const int cnt = pl.expert_cnt[s.e];
+            const Chunks ch = chunks_of(cnt);
+            const int nb = min(4, (C - s.cb * kSN) / 64);
+            // slots of the expert's last k-block; the rest of its last 16-slot group
+            // belongs to the next expert and is zeroed in both operands
+            const int rem = cnt - (ch.nk - 1) * kSK;
+            const bool ragged = ch.nk > 0 && (rem & 15) != 0;
+            for (int kc = 0; kc < ch.n && ok; ++kc) {
+                const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
+                for (int rb = s.rb0; rb < s.rb1 && ok; ++rb) {
+                    for (int kb = kb0; kb < kb1; ++kb, ++ga) {
+                        const int kbl = kb - kb0, st = ga % kAStages;
+                        const bool tail = ragged && kb == ch.nk - 1;
+                        if (rb == s.rb0) {
+                            if (!(ok = warp_wait(&S.b_full[kbl], bc & 1, abort_flag, err))) break;
+                            if (tail) {
+                                zero_tail(b_res + (size_t)kbl * kBKb, nb, rem, lane);
+                                fence_proxy_async();
+                            }
+                            __syncwarp();
+                            if (lane == 0) {
+                                mbar_arrive(&S.b_ready[kbl]);
+                                // b_ready completes once per chunk: the barriers this chunk
+                                // leaves unused get a plain arrive, after b_full[0] showed the
+                                // MMA is done with the previous chunk
+                                if (kbl == 0)
+                                    for (int k = kb1 - kb0; k < kBMaxKb; ++k) mbar_arrive(&S.b_ready[k]);
+                            }
                         }
-                        fence_proxy_async();
-                        __syncwarp();
-                    } else {
-                        int w_ok = 1;
-                        if (lane == 0) w_ok = mbar_wait(&S.full[st], par, abort_flag, err);
-                        ok = __shfl_sync(0xffffffffu, w_ok, 0) != 0;
-                        if (!ok) break;
+                        if (tail) {
+                            if (!(ok = warp_wait(&S.a_full[st], (ga / kAStages) & 1, abort_flag, err))) break;
+                            zero_tail(a_ring + (size_t)st * kAStage, 2, rem, lane);
+                            fence_proxy_async();
+                            __syncwarp();
+                        } else {
+                            int w_ok = 1;
+                            if (lane == 0) w_ok = mbar_wait(&S.a_full[st], (ga / kAStages) & 1, abort_flag, err);
+                            if (!(ok = __shfl_sync(kFull, w_ok, 0) != 0)) break;
+                        }
+                        if (lane == 0) mbar_arrive(&S.a_ready[st]);
                     }
-                    if (lane == 0) mbar_arrive(&S.fixed[st]);
                 }
+                ++bc;
             }
         }
-    } else if (warp >= 2) {
-        // ---------------- epilogue (warps 2-5) ----------------
+    } else {
+        // ---------------- epilogue (warps 2-17) ----------------
         const int q = warp & 3;                      // TMEM lane quarter
+        const int slice = (warp - 2) >> 2;           // columns [64 slice, 64 slice + 64) of the tile
         const int rr = q * 32 + lane;                // row inside the tile
         const uint32_t lane_off = ((uint32_t)(q * 32)) << 16;
-        float *my_row = rows_s + (q * 32 + lane) * kRowLd;
-        const int cw = C / 32;                       // bitmap words per storage row
         int it = 0;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            const int e = item / nrb, rb = item % nrb;
-            const int cnt = pl.expert_cnt[e];
-            const int64_t grow = (int64_t)e * R + rb * kSM + rr;   // global storage row
-            int p0 = 0, p1 = 0;
-            if (EPI == EPI_SPARSE) {
-                p0 = row_ptr[grow * 2];
-                p1 = row_ptr[grow * 2 + 1];
-            }
+        bool ok = true;
+        for (int t = t_lo; t < t_hi && ok;) {
+            const Run s = run_at(t, t_hi, nrb, pl.E);
+            t += s.rb1 - s.rb0;
+            const int cnt = pl.expert_cnt[s.e];
+            const Chunks ch = chunks_of(cnt);
+            const int c0 = s.cb * kSN;
+            // this warp's 32-column chunks of the block: [j0, j1)
+            const int nch = min(8, (C - c0) / 32);
+            const int j0 = min(nch, 2 * slice), j1 = min(nch, 2 * slice + 2);
             if (cnt == 0) {
                 // no slots: the gradient is exactly zero
-                if (EPI == EPI_SPARSE) {
-                    const int pend = row_ptr[grow * 2 + 2];
-                    for (int p = p0; p < pend; ++p) out[p] = 0.0f;
-                } else {
-                    float4 *o = reinterpret_cast<float4 *>(out + grow * C);
-                    for (int i = 0; i < C / 4; ++i) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int rb = s.rb0; rb < s.rb1; ++rb) {
+                    const int64_t grow = (int64_t)s.e * R + rb * kSM + rr;
+                    if (EPI == EPI_DENSE_ABS) {
+                        float4 *o = reinterpret_cast<float4 *>(out + grow * C + c0);
+                        for (int i = j0 * 8; i < j1 * 8; ++i) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    } else if (j0 < j1) {
+                        int q0, q1;
+                        uint2 a;
+                        slice_start(mask, cbptr, grow, C, ncb, s.cb, slice, a, q0, q1);
+                        for (int i = 0; i < __popc(a.x); ++i) out[q0 + i] = 0.0f;
+                        for (int i = 0; i < __popc(a.y); ++i) out[q1 + i] = 0.0f;
+                    }
                 }
                 continue;
             }
-            bool ok = true;
-            for (int cb = 0; cb < ncb; ++cb, ++it) {
-                const int c0 = cb * kSN;
-                const int nch = min(8, (C - c0) / 32);
-                uint32_t mw[8];
-                if (EPI == EPI_SPARSE) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) mw[j] = j < nch ? mask[grow * cw + c0 / 32 + j] : 0u;
-                }
-                const int buf = it & 1;
-                if (!mbar_wait(&S.acc_full[buf], (it >> 1) & 1, abort_flag, err)) { ok = false; break; }
-                tc_fence_after();
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    if (4 * h >= nch) break;
-                    uint32_t v[4][32];
-                    // four 32-column loads in flight, one wait (nch is a multiple of 4)
-#pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        tmem_ld_32x32b_x32(tbase + lane_off + buf * kSN + (4 * h + u) * 32, v[u]);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int j = 4 * h + u;
+            for (int kc = 0; kc < ch.n && ok; ++kc) {
+                const int mode = ch.n == 1 ? PART_ALL : kc == 0 ? PART_FIRST : kc == ch.n - 1 ? PART_LAST : PART_MID;
+                for (int rb = s.rb0; rb < s.rb1; ++rb, ++it) {
+                    const int64_t grow = (int64_t)s.e * R + rb * kSM + rr;   // global storage row
+                    uint2 mw = make_uint2(0, 0);
+                    int p0 = 0, p1 = 0;
+                    // this row's selection in the warp's two chunks and its first CSR
+                    // positions in the two halves, read before the wait
+                    if (EPI == EPI_SPARSE && j0 < j1) slice_start(mask, cbptr, grow, C, ncb, s.cb, slice, mw, p0, p1);
+                    const int buf = it & 1;
+                    if (!(ok = warp_wait(&S.acc_full[buf], (it >> 1) & 1, abort_flag, err))) break;
+                    tc_fence_after();
+                    const uint32_t tb = tbase + lane_off + buf * kSN;
+                    if (j0 < j1) {
+                        uint32_t va[32], vb[32];
+                        tmem_ld_32x32b_x32(tb + 32 * j0, va);
+                        tmem_ld_32x32b_x32(tb + 32 * j0 + 32, vb);
+                        tmem_wait_ld();
                         if (EPI == EPI_SPARSE) {
-                            uint32_t m = mw[j];
-                            if (m) {
-#pragma unroll
-                                for (int i = 0; i < 32; ++i) my_row[i] = __uint_as_float(v[u][i]);
-                                // chunk j holds columns with (c/32) % 2 == j % 2: CSR half j&1
-                                int p = (j & 1) ? p1 : p0;
-                                while (m) {
-                                    const int b = __ffs(m) - 1;
-                                    m &= m - 1;
-                                    out[p++] = round_bf16(my_row[b]);
-                                }
-                                if (j & 1) p1 = p; else p0 = p;
-                            }
+                            // chunk j holds columns with (c/32) % 2 == j % 2: CSR half j & 1
+                            // (j0 is even)
+                            drain_sparse(va, mw.x, p0, mode, out);
+                            drain_sparse(vb, mw.y, p1, mode, out);
                         } else {
-                            float4 *o = reinterpret_cast<float4 *>(out + grow * C + c0 + j * 32);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i)
-                                o[i] = make_float4(fabsf(round_bf16(__uint_as_float(v[u][4 * i]))),
-                                                   fabsf(round_bf16(__uint_as_float(v[u][4 * i + 1]))),
-                                                   fabsf(round_bf16(__uint_as_float(v[u][4 * i + 2]))),
-                                                   fabsf(round_bf16(__uint_as_float(v[u][4 * i + 3]))));
+                            float *o = out + grow * C + c0 + 32 * j0;
+                            drain_dense(va, o, mode);
+                            drain_dense(vb, o + 32, mode);
                         }
                     }
+                    tc_fence_before();
+                    mbar_arrive(&S.acc_empty[buf]);
                 }
-                tc_fence_before();
-                mbar_arrive(&S.acc_empty[buf]);
             }
-            if (!ok) break;
         }
     }
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
-    }
-}
-
-// compact[c2c[j]] += scale * g[j]   (g already rounded to the activation dtype;
-// c2c NULL: the identity map, compact kept in CSR order)
-__global__ void sddmm_accumulate(int n, const float *__restrict__ g, const int32_t *__restrict__ c2c,
-                                 float scale, float *__restrict__ compact) {
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
-        const int pos = c2c ? c2c[j] : j;
-        compact[pos] = __fadd_rn(compact[pos], __fmul_rn(scale, g[j]));
-    }
-}
-
-// the same when compact is in CSR order (identity map): 16-byte vectors for the
-// first n / 4 * 4 entries, the last n % 4 by the first threads
-__global__ void sddmm_accumulate_id(int n, const float *__restrict__ g, float scale,
-                                    float *__restrict__ compact) {
-    const int n4 = n / 4;
-    const float4 *g4 = reinterpret_cast<const float4 *>(g);
-    float4 *c4 = reinterpret_cast<float4 *>(compact);
-    const int tid = blockIdx.x * blockDim.x + threadIdx.x;
-    for (int j = tid; j < n4; j += gridDim.x * blockDim.x) {
-        const float4 a = g4[j];
-        float4 c = c4[j];
-        c.x = __fadd_rn(c.x, __fmul_rn(scale, a.x));
-        c.y = __fadd_rn(c.y, __fmul_rn(scale, a.y));
-        c.z = __fadd_rn(c.z, __fmul_rn(scale, a.z));
-        c.w = __fadd_rn(c.w, __fmul_rn(scale, a.w));
-        c4[j] = c;
-    }
-    if (tid < n - n4 * 4) {
-        const int j = n4 * 4 + tid;
-        compact[j] = __fadd_rn(compact[j], __fmul_rn(scale, g[j]));
     }
 }
 
@@ -413,7 +630,7 @@ int s_num_sms() {
 
 template <int EPI>
 int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
-                    const __nv_bfloat16 *gin, const int32_t *row_ptr, const uint32_t *mask, float *out,
+                    const __nv_bfloat16 *gin, const uint32_t *mask, const int32_t *cbptr, float *out,
                     cudaStream_t st) {
     CUtensorMap ta, tb;
     if (!s_tmap(&ta, gout, pl->P_cap, R) || !s_tmap(&tb, gin, pl->P_cap, C)) return USAF_EUNSUPPORTED;
@@ -424,9 +641,10 @@ int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16
             return USAF_ECUDA;
         attr = true;
     }
-    const int n_items = pl->E * (R / kSM);
-    dim3 grid(std::min(s_num_sms(), n_items));
-    sddmm_tc_kernel<EPI><<<grid, kSThreads, kSSmem, st>>>(ta, tb, *pl, R, C, row_ptr, mask, out);
+    const int64_t tiles = (int64_t)pl->E * (R / kSM) * ((C + kSN - 1) / kSN);
+    if (tiles == 0) return USAF_OK;
+    dim3 grid((unsigned)std::min<int64_t>(s_num_sms(), tiles));
+    sddmm_tc_kernel<EPI><<<grid, kSThreads, kSSmem, st>>>(ta, tb, *pl, R, C, mask, cbptr, out);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
@@ -434,8 +652,42 @@ int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16
 }  // namespace
 
 bool sddmm_tc_supported(int R, int C) {
-    // C % 128: a tile's column chunks come in groups of four (128 columns)
+    // C % 128: a column block is 128 or 256 columns (whole bitmap words in
+    // 16-byte loads)
     return R % kSM == 0 && C % 128 == 0 && s_encode() != nullptr;
+}
+
+// compact[c2c[j]] += scale * g[j]   (g already rounded to the activation dtype;
+// c2c NULL: the identity map, compact kept in CSR order)
+__global__ void sddmm_accumulate(int n, const float *__restrict__ g, const int32_t *__restrict__ c2c,
+                                 float scale, float *__restrict__ compact) {
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+        const int pos = c2c ? c2c[j] : j;
+        compact[pos] = __fadd_rn(compact[pos], __fmul_rn(scale, g[j]));
+    }
+}
+
+// the same when compact is in CSR order (identity map): 16-byte vectors for the
+// first n / 4 * 4 entries, the last n % 4 by the first threads
+__global__ void sddmm_accumulate_id(int n, const float *__restrict__ g, float scale,
+                                    float *__restrict__ compact) {
+    const int n4 = n / 4;
+    const float4 *g4 = reinterpret_cast<const float4 *>(g);
+    float4 *c4 = reinterpret_cast<float4 *>(compact);
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+    for (int j = tid; j < n4; j += gridDim.x * blockDim.x) {
+        const float4 a = g4[j];
+        float4 c = c4[j];
+        c.x = __fadd_rn(c.x, __fmul_rn(scale, a.x));
+        c.y = __fadd_rn(c.y, __fmul_rn(scale, a.y));
+        c.z = __fadd_rn(c.z, __fmul_rn(scale, a.z));
+        c.w = __fadd_rn(c.w, __fmul_rn(scale, a.w));
+        c4[j] = c;
+    }
+    if (tid < n - n4 * 4) {
+        const int j = n4 * 4 + tid;
+        compact[j] = __fadd_rn(compact[j], __fmul_rn(scale, g[j]));
+    }
 }
 
 // g[j] (CSR order) = bf16(D[e][r][c]) for every overlay entry, then
@@ -443,7 +695,7 @@ bool sddmm_tc_supported(int R, int C) {
 int sddmm_tc_sparse(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *gout,
                     const __nv_bfloat16 *gin, const int32_t *c2c, float scale, float *compact,
                     float *scratch, cudaStream_t st) {
-    int rc = sddmm_tc_launch<EPI_SPARSE>(pl, w->R, w->C, gout, gin, w->row_ptr, w->ov_mask, scratch, st);
+    int rc = sddmm_tc_launch<EPI_SPARSE>(pl, w->R, w->C, gout, gin, w->ov_mask, w->ov_cbptr, scratch, st);
     if (rc != USAF_OK) return rc;
     const int n = w->n_ov;
     if (!c2c && !((uintptr_t)scratch & 15) && !((uintptr_t)compact & 15)) {

@@ -238,7 +238,7 @@ extern "C" int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w
     if (w->n_ov == 0) return USAF_OK;
     USAF_REQUIRE(compact && scratch && w->row_ptr && w->col);
     cudaStream_t st = as_stream(stream);
-    const bool tc = dtype == USAF_BF16 && w->ov_mask && sddmm_tc_supported(w->R, w->C);
+    const bool tc = dtype == USAF_BF16 && w->ov_mask && w->ov_cbptr && sddmm_tc_supported(w->R, w->C);
     if (tc && !small_plan(plan))
         return sddmm_tc_sparse(plan, w, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin,
                                csr_to_compact, scale, compact, scratch, st);

@@ -142,7 +142,7 @@ class Projection:
         self.csr_to_compact = self.compact_to_csr = self.compact_to_csc = None
         self.csr_identity = False
         self.scratch = None
-        self.ov_mask = None
+        self.ov_mask = self.ov_cbptr = None
         self.qT = self.szT = self.qP = None
         if dtype == torch.bfloat16 and R % 8 == 0 and Cc % 8 == 0:
             # dequant-ordered copies for the tensor-core GEMMs (built once):
@@ -217,9 +217,14 @@ class Projection:
         self._csc_to_compact = pcsc
         # bitmap of the selected coordinates, one 32-bit word per (row, 32 columns):
         # the tensor-core gradient epilogue reads a tile's selection from it
-        self.ov_mask = None
+        self.ov_mask = self.ov_cbptr = None
         if Cc % 32 == 0:
             self.ov_mask = _bitmap((e * R + r) * (Cc // 32) + (c >> 5), c & 31, E * R * (Cc // 32))
+            # first CSR position of every 256-column block of every segment: the
+            # tensor-core epilogue starts a tile's writes there
+            self.ov_cbptr = torch.empty(E * R * ((Cc + 255) // 256) * 2, dtype=torch.int32, device=dev)
+            call("usaf_build_ov_cbptr", ptr(self.row_ptr), ptr(self.col), E, R, Cc, ptr(self.ov_cbptr),
+                 stream())
         self.val = torch.empty(n, dtype=torch.float32, device=dev)
         self.valT = torch.empty(n, dtype=torch.float32, device=dev)
         self.update_overlay_values(master)
@@ -242,6 +247,7 @@ class Projection:
                 st.colT_ptr, st.rowT, st.valT = ptr(self.colT_ptr), ptr(self.rowT), ptr(self.valT)
             st.qT, st.szT, st.qP = ptr(self.qT), ptr(self.szT), ptr(self.qP)
             st.ov_mask = ptr(self.ov_mask) if (self.n_ov and self.ov_mask is not None) else None
+            st.ov_cbptr = ptr(self.ov_cbptr) if (self.n_ov and self.ov_cbptr is not None) else None
             self._struct = st
         return self._struct
 
