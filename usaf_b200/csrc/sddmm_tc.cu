@@ -34,11 +34,12 @@
 // sums of a chunk go through fp32 in the output vector and are rounded after
 // the last chunk.
 //
-// Warp 0 issues TMA; warp 18 forwards every filled stage to the MMA after
-// zeroing the slots past an expert's end inside its last 16-slot group (they
-// belong to the next expert), so the MMA issuer -- lane 0 of warp 1, which
-// also owns TMEM -- runs a lean loop of waits, MMAs and commits (its own
-// per-k-block bookkeeping otherwise outlasts the four MMAs it issues); warps
+// Warp 0 issues TMA; warp 18 zeroes the slots past an expert's end inside its
+// last 16-slot group (they belong to the next expert) and forwards those
+// stages (and every resident gin block) to the MMA, so the MMA issuer -- lane
+// 0 of warp 1, which also owns TMEM -- runs a lean loop of waits, MMAs and
+// commits (its own per-k-block bookkeeping otherwise outlasts the four MMAs
+// it issues) and takes every other stage straight from its TMA barrier; warps
 // 2-17 drain the accumulators, four per TMEM lane quarter (64 columns each),
 // so every scheduler has four drain warps to interleave.  TMEM holds two
 // 256-column accumulators, so the drain of one tile overlaps the MMAs of the
@@ -72,7 +73,8 @@ enum : int { PART_ALL = 0, PART_FIRST = 1, PART_MID = 2, PART_LAST = 3 };
 struct alignas(8) SShared {
     uint64_t a_full[kAStages];
     uint64_t a_empty[kAStages];
-    uint64_t a_ready[kAStages];
+    uint64_t a_ready[kAStages];   // a ragged fill, zeroed by the forwarder
+    uint64_t a_tail[kAStages];    // a ragged fill was issued
     uint64_t b_full[kBMaxKb];
     uint64_t b_ready[kBMaxKb];
     uint64_t b_empty;
@@ -332,6 +334,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 mbar_init(&S.a_full[s], 1);
                 mbar_init(&S.a_empty[s], 1);
                 mbar_init(&S.a_ready[s], 1);
+                mbar_init(&S.a_tail[s], 1);
             }
             for (int k = 0; k < kBMaxKb; ++k) {
                 mbar_init(&S.b_full[k], 1);
@@ -375,6 +378,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const Chunks ch = chunks_of(cnt);
                 const int c0 = s.cb * kSN;
                 const int nb = min(4, (C - c0) / 64);
+                const bool ragged = ch.nk > 0 && ((cnt - (ch.nk - 1) * kSK) & 15) != 0;
                 for (int kc = 0; kc < ch.n && ok; ++kc) {
                     const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
                     // the previous chunk's MMAs have read the resident block
@@ -382,17 +386,16 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         ok = false;
                         break;
                     }
-                    // every b_full barrier completes once per chunk (unused ones by a
-                    // plain arrive), so their phases stay in step with the chunk count
-                    for (int k = 0; k < kBMaxKb; ++k) {
-                        if (k < kb1 - kb0) {
-                            mbar_arrive_expect_tx(&S.b_full[k], (uint32_t)(nb * kBox));
-                            const int y = row0 + (kb0 + k) * kSK;
-                            for (int j = 0; j < nb; ++j)
-                                tma_load_2d(b_res + (size_t)k * kBKb + j * kBox, &tm_in, &S.b_full[k], c0 + 64 * j, y);
-                        } else {
-                            mbar_arrive(&S.b_full[k]);
-                        }
+                    // every b_full barrier completes once per chunk, so their phases stay
+                    // in step with the chunk count: the ones this chunk leaves unused get
+                    // a plain arrive, before any load is issued (a waiter that saw
+                    // b_full[0] complete knows they have completed too)
+                    for (int k = kb1 - kb0; k < kBMaxKb; ++k) mbar_arrive(&S.b_full[k]);
+                    for (int k = 0; k < kb1 - kb0; ++k) {
+                        mbar_arrive_expect_tx(&S.b_full[k], (uint32_t)(nb * kBox));
+                        const int y = row0 + (kb0 + k) * kSK;
+                        for (int j = 0; j < nb; ++j)
+                            tma_load_2d(b_res + (size_t)k * kBKb + j * kBox, &tm_in, &S.b_full[k], c0 + 64 * j, y);
                     }
                     ++bc;
                     for (int rb = s.rb0; rb < s.rb1 && ok; ++rb) {
@@ -407,6 +410,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             const int y = row0 + kb * kSK;
                             tma_load_2d(dst, &tm_out, &S.a_full[st], rb * kSM, y);
                             tma_load_2d(dst + kBox, &tm_out, &S.a_full[st], rb * kSM + 64, y);
+                            if (ragged && kb == ch.nk - 1) mbar_arrive(&S.a_tail[st]);
                         }
                     }
                 }
@@ -424,6 +428,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
         if (lane == 0) {
             const uint32_t a_s0 = smem_u32(a_ring), b_s0 = smem_u32(b_res);
             int ga = 0, bc = 0, it = 0;
+            uint32_t tail_par = 0;   // bit st: parity of the next a_ready[st] completion
             bool ok = true;
             for (int t = t_lo; t < t_hi && ok;) {
                 const Run s = run_at(t, t_hi, nrb, pl.E);
@@ -432,6 +437,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const Chunks ch = chunks_of(cnt);
                 const int nb = min(4, (C - s.cb * kSN) / 64);
                 const uint32_t idesc = idesc_mn(kSM, nb * 64);
+                const bool ragged = ch.nk > 0 && ((cnt - (ch.nk - 1) * kSK) & 15) != 0;
                 for (int kc = 0; kc < ch.n && ok; ++kc) {
                     const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
                     for (int rb = s.rb0; rb < s.rb1 && ok; ++rb, ++it) {
@@ -442,7 +448,15 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             const int kbl = kb - kb0, st = ga % kAStages;
                             // first tile of the chunk: the resident block is in place
                             if (rb == s.rb0 && !(ok = mbar_wait(&S.b_ready[kbl], bc & 1, abort_flag, err))) break;
-                            if (!(ok = mbar_wait(&S.a_ready[st], (ga / kAStages) & 1, abort_flag, err))) break;
+                            // a stage that needs no zeroing is taken straight from the TMA
+                            // barrier; the expert's ragged last k-block comes through the
+                            // forwarder
+                            if (ragged && kb == ch.nk - 1) {
+                                if (!(ok = mbar_wait(&S.a_ready[st], (tail_par >> st) & 1, abort_flag, err))) break;
+                                tail_par ^= 1u << st;
+                            } else if (!(ok = mbar_wait(&S.a_full[st], (ga / kAStages) & 1, abort_flag, err))) {
+                                break;
+                            }
                             tc_fence_after();
                             const int nks = (min(kSK, cnt - kb * kSK) + 15) / 16;
                             const uint32_t as = a_s0 + st * kAStage, bs = b_s0 + kbl * kBKb;
@@ -467,6 +481,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     } else if (warp == kFwdWarp) {
         // ---------------- forwarder: filled stage -> MMA, tails zeroed ----------------
         int ga = 0, bc = 0;
+        uint32_t tail_par = 0;   // bit st: parity of the next a_tail[st] / a_ready[st] completion
         bool ok = true;
         for (int t = t_lo; t < t_hi && ok;) {
             const Run s = run_at(t, t_hi, nrb, pl.E);
@@ -500,17 +515,19 @@ __global__ void __launch_bounds__(kSThreads, 1)
                                     for (int k = kb1 - kb0; k < kBMaxKb; ++k) mbar_arrive(&S.b_ready[k]);
                             }
                         }
+                        // ragged fills only: a_tail says the fill was issued (so the
+                        // stage's previous fill has landed and been consumed), and
+                        // a_full cannot move past this fill before a_ready lets the
+                        // MMA consume it, so both parities are unambiguous
                         if (tail) {
+                            if (!(ok = warp_wait(&S.a_tail[st], (tail_par >> st) & 1, abort_flag, err))) break;
                             if (!(ok = warp_wait(&S.a_full[st], (ga / kAStages) & 1, abort_flag, err))) break;
                             zero_tail(a_ring + (size_t)st * kAStage, 2, rem, lane);
                             fence_proxy_async();
                             __syncwarp();
-                        } else {
-                            int w_ok = 1;
-                            if (lane == 0) w_ok = mbar_wait(&S.a_full[st], (ga / kAStages) & 1, abort_flag, err);
-                            if (!(ok = __shfl_sync(kFull, w_ok, 0) != 0)) break;
+                            if (lane == 0) mbar_arrive(&S.a_ready[st]);
+                            tail_par ^= 1u << st;
                         }
-                        if (lane == 0) mbar_arrive(&S.a_ready[st]);
                     }
                 }
                 ++bc;
