@@ -56,6 +56,12 @@ typedef struct {
     int32_t *n_pairs;     /* [1]                                               */
     int32_t *chunk_cnt;   /* [ceil(T/16)*E] scratch                            */
     int32_t *err;         /* [1]      device error word                        */
+    int32_t *sched;       /* [16] or NULL: work counters of the grouped expert
+                           * GEMMs (one pair per entry point).  Zeroed once by
+                           * the caller; every launch hands its work items out
+                           * from them longest first and leaves them zeroed.
+                           * Launches that share a plan must not overlap on
+                           * the GPU.  NULL: a fixed round-robin assignment. */
 } usaf_route_plan;
 
 /* One int4 expert projection in the usaf.quantization layout

@@ -25,7 +25,7 @@ class RoutePlan(C.Structure):
     _fields_ = [("T", I32), ("E", I32), ("P_cap", I32),
                 ("tok_cnt", P), ("tok_off", P), ("expert_cnt", P), ("expert_off", P),
                 ("seg_tok", P), ("seg_pair", P), ("seg_w", P), ("pair_exp", P),
-                ("pair_slot", P), ("n_pairs", P), ("chunk_cnt", P), ("err", P)]
+                ("pair_slot", P), ("n_pairs", P), ("chunk_cnt", P), ("err", P), ("sched", P)]
 
 
 class QWeight(C.Structure):

@@ -40,12 +40,15 @@ constexpr int kMaxTok = kSub * kMaxSub;          // 384 tokens per CTA
 constexpr int kSubBytes = kSub * kBK * 2;        // 16 KB per TMA box
 constexpr int kStageBytes = kMaxSub * kSubBytes; // 48 KB per stage
 constexpr int kAcol = kMaxTok;                   // first TMEM column of the A stages
-constexpr int kThreads = 512;  // warps 0-3 epilogue, 4 TMA, 5 MMA (+TMEM alloc), 8-15 dequant
+constexpr int kThreads = 512;  // warps 0-3 epilogue, 4 TMA + work fetch, 5 MMA (+TMEM alloc), 8-15 dequant
 constexpr int kStageLd = 136;                    // epilogue staging row stride (elements)
 
 enum : int { MODE_GATE_UP = 0, MODE_DOWN = 1, MODE_DOWN_BWD = 2, MODE_GU_BWD = 3 };
 constexpr int kBoxRows = 32;                     // token rows per TMA box
 constexpr int kBoxBytes = kBoxRows * kBK * 2;    // 4 KB
+constexpr int kQ = 3;                 // work-item queue depth
+constexpr int kQUsers = 13;           // readers of a queue slot: MMA, 8 dequant warps, 4 epilogue warps
+constexpr int kMaxOrder = 2048;       // tiles that the longest-first order can hold
 
 struct alignas(8) TcShared {
     uint64_t full_b[kStages];
@@ -53,6 +56,9 @@ struct alignas(8) TcShared {
     uint64_t empty[kStages];
     uint64_t acc;        // accumulators ready (tcgen05.commit)
     uint64_t acc_empty;  // accumulators drained by the epilogue (128 arrivals)
+    uint64_t q_full[kQ];   // a work item is in the queue slot
+    uint64_t q_empty[kQ];  // every role has read the slot
+    int item_q[kQ];        // work item, -1 = no more work
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -60,8 +66,48 @@ struct alignas(8) TcShared {
 constexpr size_t kStgBytes = (size_t)32 * kStageLd * 2;  // epilogue staging tile
 constexpr size_t kSzBytes = (size_t)4 * kBK * 4;          // transposed-mode scale ring
 // stages + epilogue staging + scale ring + shared block + tile prefix / counts (E <= 1024)
-constexpr size_t kSmemBytes =
-    (size_t)kStages * kStageBytes + kStgBytes + kSzBytes + sizeof(TcShared) + 8 * 1025 + 1024;
+// + tile order
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kStgBytes + kSzBytes + sizeof(TcShared) +
+                              8 * 1025 + 4 * kMaxOrder + 1024;
+static_assert(kSmemBytes <= 232448, "grouped GEMM shared memory above the per-block limit");
+
+// The launch's last CTA returns the work counter pair to zero for the next launch.
+__device__ __forceinline__ void sched_exit(int *c) {
+    __threadfence();
+    if (atomicAdd(c + 1, 1) == (int)gridDim.x - 1) {
+        atomicExch(c, 0);
+        atomicExch(c + 1, 0);
+        __threadfence();
+    }
+}
+
+// token-count bucket of an expert's tiles (cnt slots in ntt tiles, rounded as in decode_tile)
+__device__ __forceinline__ int tile_bucket(int cnt, int ntt) {
+    return ((((cnt + ntt - 1) / ntt) + 15) & ~15) >> 4;
+}
+
+// next work item from the CTA's queue (one thread): -1 when there is none left
+// or a wait gave up
+__device__ __forceinline__ int q_take(TcShared &S, int &qi, volatile int *abort_flag, int *err) {
+    const int slot = qi % kQ;
+    if (!mbar_wait(&S.q_full[slot], (qi / kQ) & 1, abort_flag, err)) return -1;
+    const int w = *reinterpret_cast<volatile int *>(&S.item_q[slot]);
+    mbar_arrive(&S.q_empty[slot]);
+    ++qi;
+    return w;
+}
+
+// the same for a whole warp (one arrival): -2 when the wait gave up
+__device__ __forceinline__ int q_take_warp(TcShared &S, int &qi, volatile int *abort_flag, int *err, int lane) {
+    const int slot = qi % kQ;
+    const bool ok = mbar_wait(&S.q_full[slot], (qi / kQ) & 1, abort_flag, err);
+    if (!__all_sync(0xffffffffu, ok)) return -2;
+    const int w = *reinterpret_cast<volatile int *>(&S.item_q[slot]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.q_empty[slot]);
+    ++qi;
+    return w;
+}
 
 // MODE_GATE_UP : rows = 64 gate + 64 up storage rows, K = C, SwiGLU epilogue
 //                (out0 = gu [P,R], out1 = h [P,R/2])
@@ -83,6 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     TcShared &S = *reinterpret_cast<TcShared *>(sbase + (size_t)kStages * kStageBytes + kStgBytes + kSzBytes);
     int *tile_off = reinterpret_cast<int *>(&S + 1);         // [E+1]
     int *cnts = tile_off + (pl.E + 1);                        // [E]
+    int *order = tile_off + 2 * 1025;                         // [kMaxOrder] tiles, longest first
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int R = w.R, C = w.C, E = pl.E;
@@ -128,13 +175,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             mbar_init(&S.acc, 1);
             mbar_init(&S.acc_empty, 128);
+            for (int i = 0; i < kQ; ++i) {
+                mbar_init(&S.q_full[i], 1);
+                mbar_init(&S.q_empty[i], kQUsers);
+            }
             fence_barrier_init();
         }
     }
     __syncthreads();
-    const int n_work = tile_off[E] * nrb;
-    if ((int)blockIdx.x >= n_work) return;  // whole CTA leaves before any TMEM / async work
+    const int n_tiles = tile_off[E];
+    const int n_work = n_tiles * nrb;
+    if ((int)blockIdx.x >= n_work) {   // whole CTA leaves before any TMEM / async work
+        if (tid == 0 && pl.sched) sched_exit(pl.sched + 2 * MODE);
+        return;
+    }
     volatile int *abort_flag = &S.abort_flag;
+
+    // Work items (tile, row block) are handed out longest tile first: tiles sorted
+    // by their token count in buckets of 16 slots.  The order inside a bucket is
+    // free: every item is computed whole by one CTA, so results do not depend on it.
+    const bool sorted = n_tiles <= kMaxOrder;
+    if (sorted) {
+        __shared__ int bcnt[kMaxTok / 16 + 1], bpos[kMaxTok / 16 + 1];
+        if (tid <= kMaxTok / 16) bcnt[tid] = 0;
+        __syncthreads();
+        for (int e_ = tid; e_ < E; e_ += kThreads) {
+            const int ntt = tile_off[e_ + 1] - tile_off[e_];
+            if (ntt) atomicAdd(&bcnt[tile_bucket(cnts[e_], ntt)], ntt);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int run = 0;
+            for (int b = kMaxTok / 16; b >= 0; --b) {
+                bpos[b] = run;
+                run += bcnt[b];
+            }
+        }
+        __syncthreads();
+        for (int e_ = tid; e_ < E; e_ += kThreads) {
+            const int ntt = tile_off[e_ + 1] - tile_off[e_];
+            if (ntt) {
+                const int p0 = atomicAdd(&bpos[tile_bucket(cnts[e_], ntt)], ntt);
+                for (int j = 0; j < ntt; ++j) order[p0 + j] = tile_off[e_] + j;
+            }
+        }
+        __syncthreads();
+    }
+    auto item_tile = [&](int work) { return sorted ? order[work / nrb] : work / nrb; };
 
     if (warp == 5) tmem_alloc(&S.tmem_base, 512);
     __syncthreads();
@@ -143,17 +230,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 4) {
         // ---------------- TMA producer (token rows, 32-row boxes) ----------------
+        // It also hands out the work: with plan counters each item goes to the CTA
+        // that asks next (longest first), so CTAs finish together whatever the
+        // items cost.  The next item is claimed a few k-blocks before this one's
+        // loads are all issued -- late enough that a CTA holds no work it is not
+        // about to start, early enough that the counter's latency is hidden.
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
-            int g = 0, last_g = -1;
-            for (int work = blockIdx.x; work < n_work && !*abort_flag; work += gridDim.x) {
+            int *ctr = pl.sched ? pl.sched + 2 * MODE : nullptr;
+            int fetched = 0;
+            auto fetch = [&]() {
+                const int t = ctr ? atomicAdd(ctr, 1) : (int)blockIdx.x + fetched * (int)gridDim.x;
+                ++fetched;
+                return t;
+            };
+            int g = 0, last_g = -1, qi = 0;
+            int next = fetch();
+            while (!*abort_flag) {
+                const int slot = qi % kQ;
+                if (!mbar_wait(&S.q_empty[slot], ((qi / kQ) & 1) ^ 1, abort_flag, err)) break;
+                const int work = next < n_work ? next : -1;
+                *reinterpret_cast<volatile int *>(&S.item_q[slot]) = work;
+                mbar_arrive(&S.q_full[slot]);
+                ++qi;
+                if (work < 0) break;
+                const int fetch_at = max(0, nk - 6);
                 int e, t0, ntok;
-                decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+                decode_tile(tile_off, cnts, E, item_tile(work), e, t0, ntok);
                 const int row0 = pl.expert_off[e] + t0;
                 const int nbox = (ntok + kBoxRows - 1) / kBoxRows;
                 const int rb = work % nrb;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int st = g % kStages;
+                    if (kb == fetch_at) next = fetch();
                     if (!mbar_wait(&S.empty[st], ((g / kStages) & 1) ^ 1, abort_flag, err)) break;
                     mbar_arrive_expect_tx(&S.full_b[st], (uint32_t)(nbox * kBoxBytes + (TRANS ? kBK * 4 : 0)));
                     unsigned char *dst = sbase + (size_t)st * kStageBytes;
@@ -176,10 +285,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 5) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            int g = 0, it = 0;
-            for (int work = blockIdx.x; work < n_work && !*abort_flag; work += gridDim.x, ++it) {
+            int g = 0, it = 0, qi = 0;
+            for (; !*abort_flag; ++it) {
+                const int work = q_take(S, qi, abort_flag, err);
+                if (work < 0) break;
                 int e, t0, ntok;
-                decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+                decode_tile(tile_off, cnts, E, item_tile(work), e, t0, ntok);
                 // tokens [0, 256) in one MMA of N <= 256 (columns 0..255), the rest
                 // (tokens 256..383) in a second one (columns 256..383): wide MMAs
                 // amortise the per-instruction cost of the A operand read from TMEM
@@ -223,11 +334,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kshift = __ffs(kpg) - 1;
         const unsigned short *s_ptr = reinterpret_cast<const unsigned short *>(w.s);
         const unsigned short *z_ptr = reinterpret_cast<const unsigned short *>(w.z);
-        int g = 0, it = 0;
+        int g = 0, qi = 0;
         bool ok = true;
-        for (int work = blockIdx.x; work < n_work && ok; work += gridDim.x, ++it) {
+        while (ok) {
+            const int work = q_take_warp(S, qi, abort_flag, err, lane);
+            if (work < 0) break;
             int e, t0, ntok;
-            decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+            decode_tile(tile_off, cnts, E, item_tile(work), e, t0, ntok);
             const int rb = work % nrb;
             int64_t crow;        // row of q (fwd) or qT (bwd) this lane dequantizes
             int j0 = 0, h0 = 0;  // output column base
@@ -341,10 +454,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- epilogue (warps 0-3): overlaps the next tile's dequant ----------------
         const int row = tid;                       // TMEM lane
         const uint32_t lane_off = ((uint32_t)warp * 32) << 16;
-        int it = 0;
-        for (int work = blockIdx.x; work < n_work; work += gridDim.x, ++it) {
+        int it = 0, qi = 0;
+        for (;; ++it) {
+            // one decision for the 128 epilogue threads (see below)
+            const int qs = qi % kQ;
+            if (!named_bar_and(2, 128, mbar_wait(&S.q_full[qs], (qi / kQ) & 1, abort_flag, err))) break;
+            const int work = *reinterpret_cast<volatile int *>(&S.item_q[qs]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.q_empty[qs]);
+            ++qi;
+            if (work < 0) break;
             int e, t0, ntok;
-            decode_tile(tile_off, cnts, E, work / nrb, e, t0, ntok);
+            decode_tile(tile_off, cnts, E, item_tile(work), e, t0, ntok);
             const int rb = work % nrb;
             const int row0 = pl.expert_off[e] + t0;
             int j0 = 0, h0 = 0;
@@ -478,6 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tbase, 512);
     }
+    if (tid == 0 && pl.sched) sched_exit(pl.sched + 2 * MODE);
 }
 
 // ---- host: tensor maps ------------------------------------------------------

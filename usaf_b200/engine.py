@@ -347,6 +347,7 @@ class MoEBlock:
         self.n_pairs = torch.zeros(1, **i32)
         self.chunk_cnt = torch.zeros(max(nch * E, 1), **i32)
         self.err = torch.zeros(1, **i32)
+        self.sched = torch.zeros(16, **i32)      # GEMM work counters (kernels keep them zeroed)
         self.logits = torch.empty(T, E, **f32)
         self.probs = torch.empty(T, E, **f32)
         self.wsum = torch.empty(T, **f32)
@@ -365,7 +366,7 @@ class MoEBlock:
         p = self.plan
         p.T, p.E, p.P_cap = T, E, Pc
         for name in ("tok_cnt", "tok_off", "expert_cnt", "expert_off", "seg_tok", "seg_pair",
-                     "seg_w", "pair_exp", "pair_slot", "n_pairs", "chunk_cnt", "err"):
+                     "seg_w", "pair_exp", "pair_slot", "n_pairs", "chunk_cnt", "err", "sched"):
             setattr(p, name, ptr(getattr(self, name)))
 
     # ---------------------------------------------------------------- fwd ---

@@ -150,6 +150,7 @@ class ExpertParallelMoE:
         self.own_cnt = torch.zeros(self.El, **i32)
         self.own_off = torch.zeros(self.El + 1, **i32)
         self.own_n = torch.zeros(1, **i32)
+        self.own_sched = torch.zeros(16, **i32)   # GEMM work counters of the owner plan
         self.cap = 0
         self.own = _lib.RoutePlan()
         self.xp: Optional[ExchangePlan] = None
@@ -173,6 +174,7 @@ class ExpertParallelMoE:
         p.T, p.E, p.P_cap = 0, self.El, cap
         p.expert_cnt, p.expert_off, p.n_pairs = ptr(self.own_cnt), ptr(self.own_off), ptr(self.own_n)
         p.err = ptr(self.src.err)
+        p.sched = ptr(self.own_sched)
 
     # ---------------------------------------------------------------- fwd ---
     def forward(self, x: torch.Tensor, w_r: torch.Tensor) -> torch.Tensor:
