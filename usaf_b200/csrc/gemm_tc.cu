@@ -192,31 +192,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int *abort_flag = &S.abort_flag;
 
     // Work items (tile, row block) are handed out longest tile first: tiles sorted
-    // by their token count in buckets of 16 slots.  The order inside a bucket is
-    // free: every item is computed whole by one CTA, so results do not depend on it.
+    // by their token count in buckets of 16 slots, ascending expert inside a
+    // bucket.  Every CTA must build the same order (a ticket names an item through
+    // it), so the placement is a scan, not shared-memory atomics.
     const bool sorted = n_tiles <= kMaxOrder;
     if (sorted) {
-        __shared__ int bcnt[kMaxTok / 16 + 1], bpos[kMaxTok / 16 + 1];
-        if (tid <= kMaxTok / 16) bcnt[tid] = 0;
+        constexpr int kNB = kMaxTok / 16 + 1;
+        __shared__ unsigned char bkt[1024];
+        __shared__ int bcnt[kNB], bpos[kNB];
+        if (tid < kNB) bcnt[tid] = 0;
         __syncthreads();
         for (int e_ = tid; e_ < E; e_ += kThreads) {
             const int ntt = tile_off[e_ + 1] - tile_off[e_];
-            if (ntt) atomicAdd(&bcnt[tile_bucket(cnts[e_], ntt)], ntt);
+            bkt[e_] = ntt ? (unsigned char)tile_bucket(cnts[e_], ntt) : (unsigned char)255;
+            if (ntt) atomicAdd(&bcnt[bkt[e_]], ntt);   // integer sums: the same in every CTA
         }
         __syncthreads();
         if (tid == 0) {
             int run = 0;
-            for (int b = kMaxTok / 16; b >= 0; --b) {
+            for (int b = kNB - 1; b >= 0; --b) {
                 bpos[b] = run;
                 run += bcnt[b];
             }
         }
         __syncthreads();
-        for (int e_ = tid; e_ < E; e_ += kThreads) {
-            const int ntt = tile_off[e_ + 1] - tile_off[e_];
-            if (ntt) {
-                const int p0 = atomicAdd(&bpos[tile_bucket(cnts[e_], ntt)], ntt);
-                for (int j = 0; j < ntt; ++j) order[p0 + j] = tile_off[e_] + j;
+        // one warp per bucket: the bucket's experts in ascending order, placed by a
+        // warp-wide prefix sum of their tile counts
+        for (int b = warp; b < kNB; b += kThreads / 32) {
+            int carry = bpos[b];
+            for (int e0 = 0; e0 < E; e0 += 32) {
+                const int e_ = e0 + lane;
+                const int ntt = (e_ < E && bkt[e_] == b) ? tile_off[e_ + 1] - tile_off[e_] : 0;
+                int incl = ntt;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                for (int j = 0; j < ntt; ++j) order[carry + incl - ntt + j] = tile_off[e_] + j;
+                carry += __shfl_sync(0xffffffffu, incl, 31);
             }
         }
         __syncthreads();
