@@ -274,6 +274,34 @@ __device__ __forceinline__ void drain_sparse(const uint32_t (&v)[32], uint32_t m
     }
 }
 
+// raw bitmap words and block start positions of one row's column block (the
+// loads of slice_start, issued one tile ahead of their use)
+struct SliceRaw {
+    uint4 lo, hi;
+    int2 pp;
+};
+
+__device__ __forceinline__ SliceRaw slice_load(const uint32_t *__restrict__ mask, const int32_t *__restrict__ cbptr,
+                                               int64_t grow, int C, int ncb, int cb, int slice) {
+    SliceRaw r;
+    const uint32_t *mrow = mask + grow * (C / 32) + cb * 8;
+    r.lo = __ldg(reinterpret_cast<const uint4 *>(mrow));
+    r.hi = slice >= 2 ? __ldg(reinterpret_cast<const uint4 *>(mrow) + 1) : make_uint4(0, 0, 0, 0);
+    r.pp = __ldg(reinterpret_cast<const int2 *>(cbptr + (grow * ncb + cb) * 2));
+    return r;
+}
+
+__device__ __forceinline__ void slice_decode(const SliceRaw &r, int slice, uint2 &w, int &p0, int &p1) {
+    int b0 = 0, b1 = 0;
+    if (slice >= 1) { b0 += __popc(r.lo.x); b1 += __popc(r.lo.y); }
+    if (slice >= 2) { b0 += __popc(r.lo.z); b1 += __popc(r.lo.w); }
+    if (slice >= 3) { b0 += __popc(r.hi.x); b1 += __popc(r.hi.y); }
+    w = slice == 0 ? make_uint2(r.lo.x, r.lo.y) : slice == 1 ? make_uint2(r.lo.z, r.lo.w)
+      : slice == 2 ? make_uint2(r.hi.x, r.hi.y) : make_uint2(r.hi.z, r.hi.w);
+    p0 = r.pp.x + b0;
+    p1 = r.pp.y + b1;
+}
+
 // bitmap words of chunks 2 slice and 2 slice + 1 of the row's column block
 // (w.x even chunk, w.y odd chunk) and the CSR positions where they start in
 // the row's two halves (p0 even chunks, p1 odd chunks): the block's start
@@ -426,7 +454,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (lane 0) ----------------
         if (lane == 0) {
-            const uint32_t a_s0 = smem_u32(a_ring), b_s0 = smem_u32(b_res);
+            // descriptors of the ring's and the resident block's first boxes: the
+            // start-address field (address / 16, low 14 bits) of the others is reached
+            // by adding their offset / 16 (shared addresses stay below 256 KB)
+            const uint64_t dA0 = desc_mn_sw128(smem_u32(a_ring)), dB0 = desc_mn_sw128(smem_u32(b_res));
             int ga = 0, bc = 0, it = 0;
             uint32_t tail_par = 0;   // bit st: parity of the next a_ready[st] completion
             bool ok = true;
@@ -458,11 +489,18 @@ __global__ void __launch_bounds__(kSThreads, 1)
                                 break;
                             }
                             tc_fence_after();
-                            const int nks = (min(kSK, cnt - kb * kSK) + 15) / 16;
-                            const uint32_t as = a_s0 + st * kAStage, bs = b_s0 + kbl * kBKb;
-                            for (int kk = 0; kk < nks; ++kk)
-                                mma_ss(tbase + buf * kSN, desc_mn_sw128(as + kk * 2048),
-                                       desc_mn_sw128(bs + kk * 2048), idesc, (kb > kb0 || kk > 0));
+                            const uint64_t da = dA0 + (uint64_t)((st * kAStage) >> 4);
+                            const uint64_t db = dB0 + (uint64_t)((kbl * kBKb) >> 4);
+                            const uint32_t dt = tbase + buf * kSN;
+                            if (kb < ch.nk - 1) {   // a full k-block: four MMAs
+#pragma unroll
+                                for (int kk = 0; kk < 4; ++kk)
+                                    mma_ss(dt, da + kk * (2048 >> 4), db + kk * (2048 >> 4), idesc, (kb > kb0 || kk > 0));
+                            } else {
+                                const int nks = (min(kSK, cnt - kb * kSK) + 15) / 16;
+                                for (int kk = 0; kk < nks; ++kk)
+                                    mma_ss(dt, da + kk * (2048 >> 4), db + kk * (2048 >> 4), idesc, (kb > kb0 || kk > 0));
+                            }
                             mma_commit(&S.a_empty[st]);
                         }
                         if (!ok) break;
@@ -569,28 +607,41 @@ __global__ void __launch_bounds__(kSThreads, 1)
             }
             for (int kc = 0; kc < ch.n && ok; ++kc) {
                 const int mode = ch.n == 1 ? PART_ALL : kc == 0 ? PART_FIRST : kc == ch.n - 1 ? PART_LAST : PART_MID;
+                // this row's selection in the warp's two chunks and its first CSR
+                // positions in the two halves: loaded one row block ahead, so the
+                // loads' latency hides behind a whole tile
+                const bool sel = EPI == EPI_SPARSE && j0 < j1;
+                SliceRaw nxt = {};
+                if (sel) nxt = slice_load(mask, cbptr, (int64_t)s.e * R + s.rb0 * kSM + rr, C, ncb, s.cb, slice);
                 for (int rb = s.rb0; rb < s.rb1; ++rb, ++it) {
                     const int64_t grow = (int64_t)s.e * R + rb * kSM + rr;   // global storage row
                     uint2 mw = make_uint2(0, 0);
                     int p0 = 0, p1 = 0;
-                    // this row's selection in the warp's two chunks and its first CSR
-                    // positions in the two halves, read before the wait
-                    if (EPI == EPI_SPARSE && j0 < j1) slice_start(mask, cbptr, grow, C, ncb, s.cb, slice, mw, p0, p1);
+                    if (sel) {
+                        const SliceRaw cur = nxt;
+                        if (rb + 1 < s.rb1) nxt = slice_load(mask, cbptr, grow + kSM, C, ncb, s.cb, slice);
+                        slice_decode(cur, slice, mw, p0, p1);
+                    }
                     const int buf = it & 1;
                     if (!(ok = warp_wait(&S.acc_full[buf], (it >> 1) & 1, abort_flag, err))) break;
                     tc_fence_after();
                     const uint32_t tb = tbase + lane_off + buf * kSN;
-                    if (j0 < j1) {
+                    if (j0 < j1 && EPI == EPI_SPARSE) {
+                        // chunk j holds columns with (c/32) % 2 == j % 2: CSR half j & 1
+                        // (j0 is even); one chunk in registers at a time
+                        uint32_t va[32];
+                        tmem_ld_32x32b_x32(tb + 32 * j0, va);
+                        tmem_wait_ld();
+                        drain_sparse(va, mw.x, p0, mode, out);
+                        tmem_ld_32x32b_x32(tb + 32 * j0 + 32, va);
+                        tmem_wait_ld();
+                        drain_sparse(va, mw.y, p1, mode, out);
+                    } else if (j0 < j1) {
                         uint32_t va[32], vb[32];
                         tmem_ld_32x32b_x32(tb + 32 * j0, va);
                         tmem_ld_32x32b_x32(tb + 32 * j0 + 32, vb);
                         tmem_wait_ld();
-                        if (EPI == EPI_SPARSE) {
-                            // chunk j holds columns with (c/32) % 2 == j % 2: CSR half j & 1
-                            // (j0 is even)
-                            drain_sparse(va, mw.x, p0, mode, out);
-                            drain_sparse(vb, mw.y, p1, mode, out);
-                        } else {
+                        {
                             float *o = out + grow * C + c0 + 32 * j0;
                             drain_dense(va, o, mode);
                             drain_dense(vb, o + 32, mode);
