@@ -286,6 +286,51 @@ int usaf_kth_largest(const float *vals, int64_t n, int64_t k, float *out, void *
 int usaf_expert_dense_dw(const usaf_route_plan *plan, int32_t R, int32_t C, const void *gout,
                          const void *gin, int32_t dtype, float *out, void *stream);
 
+/* Importance candidates without the dense |grad| buffer (bf16 gradients on
+ * tensor cores): the per-expert top-k of TopKImportanceStore.add
+ * (usaf/moe_loader.py:604-611, k = max(1, int(numel_e*frac*cand_mult)),
+ * experts without routed tokens contribute nothing) computed by three passes
+ * of the SDDMM over the same plan and operands as usaf_expert_dense_dw, none
+ * of which writes the gradient out.  Keys are the 15 magnitude bits of
+ * |bf16(g)| (they order like the values).  Sequence, one projection:
+ *   usaf_importance_hist(level 1)  hist[E*256] zeroed: keys by exponent;
+ *   usaf_importance_pick(level 1)  pval[e], need[e];
+ *   usaf_importance_hist(level 2)  hist zeroed again: the keys of bucket pval[e];
+ *   usaf_importance_pick(level 2)  thr[e] (the k-th largest key), n_eq[e] keys
+ *                                  equal to it, need[e] of those to take;
+ *   usaf_importance_emit           keys > thr[e] into candidate row
+ *                                  cand_row[e] (k entries a row), keys == thr[e]
+ *                                  into the tie list at eq_off[e] (exclusive
+ *                                  scan of n_eq); n_gt / n_eq zeroed first;
+ *   usaf_sort_u32 of the tie lists by flat index (usaf_importance_keys mode 0
+ *   builds the keys, mode 2 gathers), then usaf_importance_take_ties appends
+ *   the need[e] lowest-index ties to each row;
+ *   usaf_importance_keys mode 0 + usaf_sort_u32, then mode 1 + usaf_sort_u32,
+ *   then mode 2: rows ordered by descending value, ties by ascending index.
+ * part / part_slot: fp32 partial sums [n * R * C] of the experts with more
+ * than usaf_importance_chunk_slots() slots (part_slot[e] their slot, -1 for
+ * the rest; may be NULL when no expert has that many).  cand_row[e] < 0 or
+ * thr[e] < 0 leaves expert e out.  Flat indices are e*R*C + r*C + c. */
+int32_t usaf_importance_chunk_slots(void);
+int usaf_importance_supported(int32_t R, int32_t C, int32_t dtype);
+int usaf_importance_hist(const usaf_route_plan *plan, int32_t R, int32_t C, const void *gout,
+                         const void *gin, int32_t dtype, int32_t level, const int32_t *pval,
+                         uint32_t *hist, float *part, const int32_t *part_slot, void *stream);
+int usaf_importance_pick(const uint32_t *hist, int32_t E, int64_t k, const int32_t *expert_cnt,
+                         int32_t level, int32_t *pval, int64_t *need, int32_t *thr, int64_t *n_eq,
+                         void *stream);
+int usaf_importance_emit(const usaf_route_plan *plan, int32_t R, int32_t C, const void *gout,
+                         const void *gin, int32_t dtype, const int32_t *thr, int64_t k,
+                         const int32_t *cand_row, int32_t *n_gt, int32_t *n_eq, float *cand_val,
+                         int64_t *cand_idx, const int64_t *eq_off, float *eq_val, int64_t *eq_idx,
+                         float *part, const int32_t *part_slot, void *stream);
+int usaf_importance_take_ties(int32_t E, int64_t k, const int32_t *cand_row, const int64_t *need,
+                              const int64_t *eq_off, const float *eq_val, const int64_t *eq_idx,
+                              float *cand_val, int64_t *cand_idx, void *stream);
+int usaf_importance_keys(const float *val, const int64_t *idx, const int64_t *perm, int64_t n,
+                         int64_t k, int32_t mode, float *val_out, int64_t *idx_out, uint32_t *keys,
+                         int64_t *pos, void *stream);
+
 /* usaf_sort_u32: stable LSD radix sort of (uint32 key, int64 payload) pairs,
  * ascending (descending != 0: descending) by key; equal keys keep input
  * order.  Used to build the overlay CSR/CSC from selected flat indices.

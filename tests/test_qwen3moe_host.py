@@ -154,6 +154,12 @@ class _StandInEP:
         R, C = (2 * 16, 32) if which == "gate_up_proj" else (32, 16)
         return torch.ones(self.El, R, C)
 
+    def hit_experts(self):
+        return (self.own_cnt > 0).nonzero().reshape(-1)
+
+    def expert_candidates(self, which, k):
+        return None   # no device gradients here: the store takes the dense |grad| path
+
 
 def test_expert_parallel_block_glue(monkeypatch):
     """attach(expert_parallel=True) sends the block through the expert-parallel

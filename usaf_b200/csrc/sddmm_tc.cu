@@ -14,6 +14,19 @@
 //                  scale * that value to the compact vector.
 //   EPI_DENSE_ABS: |dtype(D)| at every coordinate (importance pass,
 //                  usaf/importance.py).
+//   EPI_HIST     : the importance candidates without writing D out
+//                  (TopKImportanceStore, usaf/moe_loader.py:604-611): a
+//                  histogram per expert of the 15-bit keys of |bf16(D)|
+//                  (exponent and mantissa bits, ordered like the values),
+//                  restricted to the keys with a given prefix, counted in
+//                  per-warp shared-memory histograms and folded into global
+//                  memory once per run of tiles;
+//   EPI_EMIT     : the same keys against a threshold per expert: every
+//                  coordinate above it goes to the expert's candidate list,
+//                  every one equal to it to the expert's tie list.
+//   Experts whose slots span several chunks keep their partial sums in
+//   fp32 (in `out` for EPI_DENSE_ABS, in a caller scratch for the
+//   importance modes).
 //
 // Tile = 128 storage rows x 256 columns (MMA M x N), K = the expert's slots in
 // blocks of 64.  Both operands reach shared memory as TMA boxes of 64 slots x
@@ -66,7 +79,8 @@ constexpr int kAStage = 2 * kBox;        // 128 rows
 constexpr int kBKb = 4 * kBox;           // 256 columns
 constexpr uint32_t kFull = 0xffffffffu;
 
-enum : int { EPI_SPARSE = 0, EPI_DENSE_ABS = 1 };
+enum : int { EPI_SPARSE = 0, EPI_DENSE_ABS = 1, EPI_HIST = 2, EPI_EMIT = 3 };
+constexpr int kHistBins = 256;
 // how a tile's sums combine with the other slot chunks of its expert
 enum : int { PART_ALL = 0, PART_FIRST = 1, PART_MID = 2, PART_LAST = 3 };
 
@@ -130,7 +144,7 @@ __device__ __forceinline__ float round_bf16(float v) {
 // cost of one tile of an expert with `cnt` slots, in units of one 16-slot MMA
 // step (the fixed part stands for the epilogue and the stream of gout)
 __device__ __forceinline__ int64_t tile_cost(int cnt, int dense) {
-    if (cnt <= 0) return dense ? 40 : 2;
+    if (cnt <= 0) return dense == 2 ? 0 : dense ? 40 : 2;
     return (cnt + 15) / 16 + (dense ? 40 : 6);
 }
 
@@ -340,16 +354,122 @@ __device__ __forceinline__ void drain_dense(const uint32_t (&v)[32], float *o, i
     }
 }
 
+// ---- importance epilogues ---------------------------------------------------
+
+// Arguments of EPI_HIST / EPI_EMIT (zero for the other modes).
+struct ImpArgs {
+    int shift, pmask;            // HIST: key counted in bin (key >> shift) & 255 if (key & pmask) == pval[e]
+    const int32_t *pval;         // [E]
+    unsigned int *hist;          // [E * 256]
+    const int32_t *thr;          // EMIT: [E] threshold key, < 0: the expert emits nothing
+    int64_t k;                   // EMIT: candidate list capacity per expert
+    const int32_t *cand_row;     // EMIT: [E] first row of e's candidate list (in units of k)
+    int32_t *n_gt, *n_eq;        // EMIT: [E] list fills (zeroed by the caller)
+    float *gt_val;               // EMIT: candidate values / flat indices
+    int64_t *gt_idx;
+    const int64_t *eq_off;       // EMIT: [E] start of e's tie list
+    float *eq_val;
+    int64_t *eq_idx;
+    float *part;                 // fp32 partial sums of experts that take several chunks
+    const int32_t *part_slot;    // [E] their slot in `part`, -1 for the others
+};
+
+// 15-bit order key of |bf16(v)|: exponent and mantissa bits of the rounded value
+__device__ __forceinline__ int abs_key(float v) {
+    return (int)((__float_as_uint(round_bf16(v)) >> 16) & 0x7FFFu);
+}
+
+// the final value of one 32-column chunk of a row (partials of earlier chunks
+// added), or nothing when this chunk is not the expert's last
+__device__ __forceinline__ bool chunk_final(uint32_t (&v)[32], float *part_row, int mode) {
+    if (mode == PART_ALL) return true;
+    float4 *o4 = reinterpret_cast<float4 *>(part_row);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float4 a = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+        if (mode != PART_FIRST) {
+            const float4 b = o4[i];
+            a = make_float4(__fadd_rn(b.x, a.x), __fadd_rn(b.y, a.y), __fadd_rn(b.z, a.z), __fadd_rn(b.w, a.w));
+        }
+        if (mode == PART_LAST) {
+            v[4 * i] = __float_as_uint(a.x);
+            v[4 * i + 1] = __float_as_uint(a.y);
+            v[4 * i + 2] = __float_as_uint(a.z);
+            v[4 * i + 3] = __float_as_uint(a.w);
+        } else {
+            o4[i] = a;
+        }
+    }
+    return mode == PART_LAST;
+}
+
+__device__ __forceinline__ void hist_chunk(const uint32_t (&v)[32], unsigned int *h, int shift, int pmask, int pv) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const int key = abs_key(__uint_as_float(v[i]));
+        if ((key & pmask) == pv) atomicAdd(&h[(key >> shift) & (kHistBins - 1)], 1u);
+    }
+}
+
+// candidates of one chunk: the warp reserves list room with one atomic per list,
+// every lane then stores its own entries in column order
+__device__ __forceinline__ void emit_chunk(const uint32_t (&v)[32], int e, int64_t flat0, int thr,
+                                           const ImpArgs &ia, int lane) {
+    uint32_t mg = 0, me = 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const int key = abs_key(__uint_as_float(v[i]));
+        mg |= (uint32_t)(key > thr) << i;
+        me |= (uint32_t)(key == thr) << i;
+    }
+    const int ng = __popc(mg), ne = __popc(me);
+    int sg = ng, se = ne;   // inclusive scans over the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int yg = __shfl_up_sync(kFull, sg, o), ye = __shfl_up_sync(kFull, se, o);
+        if (lane >= o) { sg += yg; se += ye; }
+    }
+    int bg = 0, be = 0;
+    if (lane == 31) {
+        if (sg) bg = atomicAdd(ia.n_gt + e, sg);
+        if (se) be = atomicAdd(ia.n_eq + e, se);
+    }
+    bg = __shfl_sync(kFull, bg, 31) + sg - ng;
+    be = __shfl_sync(kFull, be, 31) + se - ne;
+    if (!(ng | ne)) return;
+    float *gv = ia.gt_val + (int64_t)ia.cand_row[e] * ia.k;
+    int64_t *gi = ia.gt_idx + (int64_t)ia.cand_row[e] * ia.k;
+    float *ev = ia.eq_val + ia.eq_off[e];
+    int64_t *ei = ia.eq_idx + ia.eq_off[e];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float a = fabsf(round_bf16(__uint_as_float(v[i])));
+        if ((mg >> i) & 1u) {
+            gv[bg] = a;
+            gi[bg] = flat0 + i;
+            ++bg;
+        }
+        if ((me >> i) & 1u) {
+            ev[be] = a;
+            ei[be] = flat0 + i;
+            ++be;
+        }
+    }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kSThreads, 1)
     sddmm_tc_kernel(const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_in,
                     usaf_route_plan pl, int R, int C, const uint32_t *__restrict__ mask,
-                    const int32_t *__restrict__ cbptr, float *__restrict__ out) {
+                    const int32_t *__restrict__ cbptr, float *__restrict__ out, const ImpArgs ia) {
+    // the histogram mode gives up one gout stage for the per-warp histograms
+    constexpr int AST = EPI == EPI_HIST ? kAStages - 1 : kAStages;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *sb = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char *a_ring = sb;
-    unsigned char *b_res = sb + (size_t)kAStages * kAStage;
+    unsigned char *b_res = sb + (size_t)kAStages * kAStage;   // the layout keeps every stage
     SShared &S = *reinterpret_cast<SShared *>(b_res + (size_t)kBMaxKb * kBKb);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nrb = R / kSM;
@@ -358,7 +478,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     if (warp == 0) {
         if (lane == 0) {
             S.abort_flag = 0;
-            for (int s = 0; s < kAStages; ++s) {
+            for (int s = 0; s < kAStages; ++s) {   // (all barriers exist)
                 mbar_init(&S.a_full[s], 1);
                 mbar_init(&S.a_empty[s], 1);
                 mbar_init(&S.a_ready[s], 1);
@@ -377,7 +497,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
             fence_barrier_init();
         }
         int lo, hi;
-        tile_range(pl, nrb, ncb, EPI == EPI_DENSE_ABS, lane, &lo, &hi);
+        tile_range(pl, nrb, ncb, EPI == EPI_SPARSE ? 0 : EPI == EPI_DENSE_ABS ? 1 : 2, lane, &lo, &hi);
         if (lane == 0) {
             S.t_lo = lo;
             S.t_hi = hi;
@@ -428,8 +548,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
                     ++bc;
                     for (int rb = s.rb0; rb < s.rb1 && ok; ++rb) {
                         for (int kb = kb0; kb < kb1; ++kb, ++ga) {
-                            const int st = ga % kAStages;
-                            if (!mbar_wait(&S.a_empty[st], ((ga / kAStages) & 1) ^ 1, abort_flag, err)) {
+                            const int st = ga % AST;
+                            if (!mbar_wait(&S.a_empty[st], ((ga / AST) & 1) ^ 1, abort_flag, err)) {
                                 ok = false;
                                 break;
                             }
@@ -445,8 +565,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
             }
             if (*abort_flag) {
                 // loads in flight land before the CTA's shared memory is released
-                for (int g = max(0, ga - kAStages); g < ga; ++g)
-                    s_drain(&S.a_full[g % kAStages], (g / kAStages) & 1, err);
+                for (int g = max(0, ga - AST); g < ga; ++g)
+                    s_drain(&S.a_full[g % AST], (g / AST) & 1, err);
                 if (bc > 0)
                     for (int k = 0; k < kBMaxKb; ++k) s_drain(&S.b_full[k], (bc - 1) & 1, err);
             }
@@ -476,7 +596,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         if (!(ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err))) break;
                         tc_fence_after();
                         for (int kb = kb0; kb < kb1; ++kb, ++ga) {
-                            const int kbl = kb - kb0, st = ga % kAStages;
+                            const int kbl = kb - kb0, st = ga % AST;
                             // first tile of the chunk: the resident block is in place
                             if (rb == s.rb0 && !(ok = mbar_wait(&S.b_ready[kbl], bc & 1, abort_flag, err))) break;
                             // a stage that needs no zeroing is taken straight from the TMA
@@ -485,7 +605,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             if (ragged && kb == ch.nk - 1) {
                                 if (!(ok = mbar_wait(&S.a_ready[st], (tail_par >> st) & 1, abort_flag, err))) break;
                                 tail_par ^= 1u << st;
-                            } else if (!(ok = mbar_wait(&S.a_full[st], (ga / kAStages) & 1, abort_flag, err))) {
+                            } else if (!(ok = mbar_wait(&S.a_full[st], (ga / AST) & 1, abort_flag, err))) {
                                 break;
                             }
                             tc_fence_after();
@@ -535,7 +655,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
                 for (int rb = s.rb0; rb < s.rb1 && ok; ++rb) {
                     for (int kb = kb0; kb < kb1; ++kb, ++ga) {
-                        const int kbl = kb - kb0, st = ga % kAStages;
+                        const int kbl = kb - kb0, st = ga % AST;
                         const bool tail = ragged && kb == ch.nk - 1;
                         if (rb == s.rb0) {
                             if (!(ok = warp_wait(&S.b_full[kbl], bc & 1, abort_flag, err))) break;
@@ -559,7 +679,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         // MMA consume it, so both parities are unambiguous
                         if (tail) {
                             if (!(ok = warp_wait(&S.a_tail[st], (tail_par >> st) & 1, abort_flag, err))) break;
-                            if (!(ok = warp_wait(&S.a_full[st], (ga / kAStages) & 1, abort_flag, err))) break;
+                            if (!(ok = warp_wait(&S.a_full[st], (ga / AST) & 1, abort_flag, err))) break;
                             zero_tail(a_ring + (size_t)st * kAStage, 2, rem, lane);
                             fence_proxy_async();
                             __syncwarp();
@@ -577,6 +697,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
         const int slice = (warp - 2) >> 2;           // columns [64 slice, 64 slice + 64) of the tile
         const int rr = q * 32 + lane;                // row inside the tile
         const uint32_t lane_off = ((uint32_t)(q * 32)) << 16;
+        // importance histogram: one 256-bin copy per drain warp in the unused gout stage
+        unsigned int *hist_all = reinterpret_cast<unsigned int *>(a_ring + (size_t)(kAStages - 1) * kAStage);
+        unsigned int *hw = hist_all + (warp - 2) * kHistBins;
+        const int et = tid - 64;   // 0..511 over the drain warps
+        if (EPI == EPI_HIST) {
+            for (int i = et; i < 16 * kHistBins; i += kEpiThreads) hist_all[i] = 0u;
+            named_bar_sync(1, kEpiThreads);
+        }
         int it = 0;
         bool ok = true;
         for (int t = t_lo; t < t_hi && ok;) {
@@ -588,6 +716,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
             // this warp's 32-column chunks of the block: [j0, j1)
             const int nch = min(8, (C - c0) / 32);
             const int j0 = min(nch, 2 * slice), j1 = min(nch, 2 * slice + 2);
+            // importance: an expert without slots has no gradient hook in the reference
+            // (and a threshold below zero means the caller left the expert out)
+            if (EPI >= EPI_HIST && (cnt == 0 || (EPI == EPI_EMIT && ia.thr[s.e] < 0) ||
+                                    (EPI == EPI_HIST && ia.pmask && ia.pval[s.e] < 0)))
+                continue;
             if (cnt == 0) {
                 // no slots: the gradient is exactly zero
                 for (int rb = s.rb0; rb < s.rb1; ++rb) {
@@ -636,6 +769,21 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         tmem_ld_32x32b_x32(tb + 32 * j0 + 32, va);
                         tmem_wait_ld();
                         drain_sparse(va, mw.y, p1, mode, out);
+                    } else if (j0 < j1 && EPI >= EPI_HIST) {
+                        const int64_t lrow = (int64_t)rb * kSM + rr;   // row inside the expert
+                        float *prow = mode == PART_ALL ? nullptr
+                                    : ia.part + ((int64_t)ia.part_slot[s.e] * R + lrow) * C + c0 + 32 * j0;
+                        const int64_t flat0 = ((int64_t)s.e * R + lrow) * C + c0 + 32 * j0;
+#pragma unroll 1
+                        for (int h = 0; h < 2; ++h) {
+                            uint32_t va[32];
+                            tmem_ld_32x32b_x32(tb + 32 * (j0 + h), va);
+                            tmem_wait_ld();
+                            if (chunk_final(va, prow + 32 * h, mode)) {
+                                if (EPI == EPI_HIST) hist_chunk(va, hw, ia.shift, ia.pmask, ia.pmask ? ia.pval[s.e] : 0);
+                                else emit_chunk(va, s.e, flat0 + 32 * h, ia.thr[s.e], ia, lane);
+                            }
+                        }
                     } else if (j0 < j1) {
                         uint32_t va[32], vb[32];
                         tmem_ld_32x32b_x32(tb + 32 * j0, va);
@@ -650,6 +798,22 @@ __global__ void __launch_bounds__(kSThreads, 1)
                     tc_fence_before();
                     mbar_arrive(&S.acc_empty[buf]);
                 }
+            }
+            if (EPI == EPI_HIST) {
+                // the run's counts (one expert) into its global histogram; every drain
+                // warp gets here, and all take the same decision on a wait that gave up
+                ok = named_bar_and(1, kEpiThreads, ok);
+                if (!ok) break;
+                if (et < kHistBins) {
+                    unsigned int sum = 0;
+#pragma unroll 4
+                    for (int w = 0; w < 16; ++w) {
+                        sum += hist_all[w * kHistBins + et];
+                        hist_all[w * kHistBins + et] = 0u;
+                    }
+                    if (sum) atomicAdd(ia.hist + (int64_t)s.e * kHistBins + et, sum);
+                }
+                named_bar_sync(1, kEpiThreads);
             }
         }
     }
@@ -699,7 +863,7 @@ int s_num_sms() {
 template <int EPI>
 int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
                     const __nv_bfloat16 *gin, const uint32_t *mask, const int32_t *cbptr, float *out,
-                    cudaStream_t st) {
+                    cudaStream_t st, const ImpArgs &ia = ImpArgs{}) {
     CUtensorMap ta, tb;
     if (!s_tmap(&ta, gout, pl->P_cap, R) || !s_tmap(&tb, gin, pl->P_cap, C)) return USAF_EUNSUPPORTED;
     static bool attr = false;
@@ -712,7 +876,7 @@ int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16
     const int64_t tiles = (int64_t)pl->E * (R / kSM) * ((C + kSN - 1) / kSN);
     if (tiles == 0) return USAF_OK;
     dim3 grid((unsigned)std::min<int64_t>(s_num_sms(), tiles));
-    sddmm_tc_kernel<EPI><<<grid, kSThreads, kSSmem, st>>>(ta, tb, *pl, R, C, mask, cbptr, out);
+    sddmm_tc_kernel<EPI><<<grid, kSThreads, kSSmem, st>>>(ta, tb, *pl, R, C, mask, cbptr, out, ia);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
@@ -781,5 +945,47 @@ int sddmm_tc_dense_abs(const usaf_route_plan *pl, int R, int C, const __nv_bfloa
                        const __nv_bfloat16 *gin, float *out, cudaStream_t st) {
     return sddmm_tc_launch<EPI_DENSE_ABS>(pl, R, C, gout, gin, nullptr, nullptr, out, st);
 }
+
+// importance histogram pass: hist[e][(key >> shift) & 255] += 1 for every key of
+// expert e with (key & pmask) == pval[e] (experts without slots are skipped)
+int sddmm_tc_key_hist(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
+                      const __nv_bfloat16 *gin, int shift, int pmask, const int32_t *pval,
+                      unsigned int *hist, float *part, const int32_t *part_slot, cudaStream_t st) {
+    ImpArgs ia{};
+    ia.shift = shift;
+    ia.pmask = pmask;
+    ia.pval = pval;
+    ia.hist = hist;
+    ia.part = part;
+    ia.part_slot = part_slot;
+    return sddmm_tc_launch<EPI_HIST>(pl, R, C, gout, gin, nullptr, nullptr, nullptr, st, ia);
+}
+
+// importance emit pass: coordinates of expert e with key > thr[e] into its
+// candidate list (row cand_row[e] of gt_val / gt_idx, k entries a row), those
+// with key == thr[e] into its tie list at eq_off[e]; experts with thr < 0 skipped
+int sddmm_tc_key_emit(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
+                      const __nv_bfloat16 *gin, const int32_t *thr, int64_t k, const int32_t *cand_row,
+                      int32_t *n_gt, int32_t *n_eq, float *gt_val, int64_t *gt_idx, const int64_t *eq_off,
+                      float *eq_val, int64_t *eq_idx, float *part, const int32_t *part_slot, cudaStream_t st) {
+    ImpArgs ia{};
+    ia.thr = thr;
+    ia.k = k;
+    ia.cand_row = cand_row;
+    ia.n_gt = n_gt;
+    ia.n_eq = n_eq;
+    ia.gt_val = gt_val;
+    ia.gt_idx = gt_idx;
+    ia.eq_off = eq_off;
+    ia.eq_val = eq_val;
+    ia.eq_idx = eq_idx;
+    ia.part = part;
+    ia.part_slot = part_slot;
+    return sddmm_tc_launch<EPI_EMIT>(pl, R, C, gout, gin, nullptr, nullptr, nullptr, st, ia);
+}
+
+// slots above which an expert's gradient is summed over several chunks (the
+// importance passes then keep its partial sums in the caller's scratch)
+int sddmm_tc_chunk_slots() { return kBMaxKb * kSK; }
 
 }  // namespace usaf

@@ -46,6 +46,87 @@ def sort_u32(keys: torch.Tensor, payload: torch.Tensor, descending: bool = False
     return kout, vout
 
 
+def expert_candidates(plan, expert_cnt: torch.Tensor, R: int, C: int, gout: torch.Tensor,
+                      gin: torch.Tensor, dtc: int, k: int):
+    """Per-expert top ``k`` of |grad_e| (TopKImportanceStore.add,
+    usaf/moe_loader.py:604-611) for every expert with routed slots, without
+    forming the dense gradient: three tensor-core SDDMM passes (exponent
+    histogram, histogram inside the threshold bucket, emission) and device
+    sorts.  Returns ``(vals, idx, experts)``: rows of ``k`` scores (descending,
+    ties by ascending flat index) and flat indices ``e*R*C + r*C + c``, one row
+    per entry of ``experts``; or None when the fused path does not cover the
+    shape or dtype (the caller then uses the dense |grad| path)."""
+    if not _lib.LIB.usaf_importance_supported(R, C, dtc):
+        return None
+    dev = gout.device
+    E = expert_cnt.numel()
+    cnt_h = expert_cnt.cpu()
+    experts = (cnt_h > 0).nonzero().reshape(-1)
+    n_act = experts.numel()
+    i32 = dict(dtype=torch.int32, device=dev)
+    i64 = dict(dtype=torch.int64, device=dev)
+    if n_act == 0:
+        return (torch.empty(0, dtype=torch.float32, device=dev), torch.empty(0, **i64), experts)
+    cand_row = torch.full((E,), -1, dtype=torch.int32)
+    cand_row[experts] = torch.arange(n_act, dtype=torch.int32)
+    cand_row = cand_row.to(dev)
+    # fp32 partial sums of the experts whose slots span several SDDMM chunks
+    big = (cnt_h > int(_lib.LIB.usaf_importance_chunk_slots())).nonzero().reshape(-1)
+    part = part_slot = None
+    if big.numel():
+        ps = torch.full((E,), -1, dtype=torch.int32)
+        ps[big] = torch.arange(big.numel(), dtype=torch.int32)
+        part_slot = ps.to(dev)
+        part = torch.empty(big.numel() * R * C, dtype=torch.float32, device=dev)
+    st = stream()
+    hist = torch.zeros(E * 256, **i32)
+    pval = torch.empty(E, **i32)
+    need = torch.empty(E, **i64)
+    thr = torch.empty(E, **i32)
+    n_eq = torch.empty(E, **i64)
+    args = (ptr(gout), ptr(gin), dtc)
+    call("usaf_importance_hist", plan, R, C, *args, 1, None, ptr(hist), ptr(part), ptr(part_slot), st)
+    call("usaf_importance_pick", ptr(hist), E, k, ptr(expert_cnt), 1, ptr(pval), ptr(need), None, None, st)
+    hist.zero_()
+    call("usaf_importance_hist", plan, R, C, *args, 2, ptr(pval), ptr(hist), ptr(part), ptr(part_slot), st)
+    call("usaf_importance_pick", ptr(hist), E, k, None, 2, ptr(pval), ptr(need), ptr(thr), ptr(n_eq), st)
+    eq_off = torch.cumsum(n_eq, 0) - n_eq
+    n_ties = int(n_eq.sum())                       # host read: sizes the tie lists
+    n = n_act * k
+    vals = torch.empty(n, dtype=torch.float32, device=dev)
+    idx = torch.empty(n, **i64)
+    eq_val = torch.empty(max(n_ties, 1), dtype=torch.float32, device=dev)
+    eq_idx = torch.empty(max(n_ties, 1), **i64)
+    n_gt = torch.zeros(E, **i32)
+    n_eqc = torch.zeros(E, **i32)
+    call("usaf_importance_emit", plan, R, C, *args, ptr(thr), k, ptr(cand_row), ptr(n_gt), ptr(n_eqc),
+         ptr(vals), ptr(idx), ptr(eq_off), ptr(eq_val), ptr(eq_idx), ptr(part), ptr(part_slot), st)
+    if n_ties:
+        # ties at the threshold resolve to the lowest flat index: order the tie
+        # lists by index and take each expert's first need[e]
+        keys = torch.empty(n_ties, **i32)
+        pos = torch.empty(n_ties, **i64)
+        call("usaf_importance_keys", ptr(eq_val), ptr(eq_idx), None, n_ties, 1, 0, None, None, ptr(keys),
+             ptr(pos), st)
+        _, perm = sort_u32(keys, pos)
+        ev, ei = torch.empty_like(eq_val), torch.empty_like(eq_idx)
+        call("usaf_importance_keys", ptr(eq_val), ptr(eq_idx), ptr(perm), n_ties, 1, 2, ptr(ev), ptr(ei),
+             None, None, st)
+        call("usaf_importance_take_ties", E, k, ptr(cand_row), ptr(need), ptr(eq_off), ptr(ev), ptr(ei),
+             ptr(vals), ptr(idx), st)
+    # rows by descending score, equal scores by ascending index: sort by index,
+    # then stably by (row, descending score)
+    keys = torch.empty(n, **i32)
+    pos = torch.empty(n, **i64)
+    call("usaf_importance_keys", ptr(vals), ptr(idx), None, n, k, 0, None, None, ptr(keys), ptr(pos), st)
+    _, perm = sort_u32(keys, pos)
+    v1, i1 = torch.empty_like(vals), torch.empty_like(idx)
+    call("usaf_importance_keys", ptr(vals), ptr(idx), ptr(perm), n, k, 1, ptr(v1), ptr(i1), ptr(keys), ptr(pos), st)
+    _, perm = sort_u32(keys, pos)
+    call("usaf_importance_keys", ptr(v1), ptr(i1), ptr(perm), n, k, 2, ptr(vals), ptr(idx), None, None, st)
+    return vals, idx, experts
+
+
 def build_rowptr(rows: torch.Tensor, n_rows: int) -> torch.Tensor:
     rows = rows.to(torch.int64).contiguous()
     out = torch.empty(n_rows + 1, dtype=torch.int32, device=rows.device)
@@ -464,6 +545,20 @@ class MoEBlock:
         if dn.n_ov:
             call("usaf_sparse_dw", self.plan, dn.struct(), ptr(self.dcur), ptr(self.h),
                  self.dtc, _map(dn), scale, ptr(compact_dn), ptr(dn.scratch), st)
+
+    def hit_experts(self) -> torch.Tensor:
+        """Experts with routed slots in the last forward."""
+        return (self.expert_cnt > 0).nonzero().reshape(-1)
+
+    def expert_candidates(self, which: str, k: int):
+        """Per-expert top-``k`` |dW| candidates of one projection without the
+        dense buffer (see :func:`expert_candidates`); None if not covered."""
+        d = self.d
+        if which == "gate_up_proj":
+            R, Cc, gout, gin = 2 * d.I, d.H, self.dgu, self.x_perm
+        else:
+            R, Cc, gout, gin = d.H, d.I, self.dcur, self.h
+        return expert_candidates(self.plan, self.expert_cnt, R, Cc, gout, gin, self.dtc, k)
 
     def dense_abs_grad(self, which: str) -> torch.Tensor:
         """|dW| of every expert of one projection as fp32 [E, R, C] (importance)."""

@@ -25,7 +25,7 @@ import torch.distributed as dist
 
 from . import _lib
 from ._lib import call, ptr, stream
-from .engine import BlockDims, MoEBlock, Projection, _check_act, _map
+from .engine import BlockDims, MoEBlock, Projection, _check_act, _map, expert_candidates
 from .moe_loader import SparseGradStore, TopKImportanceStore, select_candidates
 from .sparse_optim import SparseAdam
 
@@ -247,6 +247,19 @@ class ExpertParallelMoE:
             call("usaf_sparse_dw", self.own, self.dn.struct(), ptr(self.dcur_own), ptr(self.h_own),
                  self.dtc, _map(self.dn), scale, ptr(compact_dn), ptr(self.dn.scratch), st)
 
+    def hit_experts(self) -> torch.Tensor:
+        """This rank's experts that received slots from any rank."""
+        return (self.own_cnt > 0).nonzero().reshape(-1)
+
+    def expert_candidates(self, which: str, k: int):
+        """Per-expert top-``k`` |dW| candidates of this rank's experts (all
+        ranks' tokens) without the dense buffer; None if not covered."""
+        if which == "gate_up_proj":
+            R, C, gout, gin = 2 * self.I, self.H, self.dgu_own, self.x_own
+        else:
+            R, C, gout, gin = self.H, self.I, self.dcur_own, self.h_own
+        return expert_candidates(self.own, self.own_cnt, R, C, gout, gin, self.dtc, k)
+
     def dense_abs_grad(self, which: str) -> torch.Tensor:
         """|dW| of this rank's experts (fp32 [El, R, C]) for the importance pass."""
         if which == "gate_up_proj":
@@ -322,9 +335,8 @@ class ExpertParallelLayer:
         m.forward(x, self.w_r)
         m.backward(dy, x, self.w_r, reduce_router=False)
         store = TopKImportanceStore(self.full_shapes, frac, cand_mult)
-        hit = (m.own_cnt > 0).nonzero().reshape(-1)
         for name in self.names:
-            store.add_dense_abs(name, m.dense_abs_grad(self.which[name]), hit, expert_offset=self.e0)
+            store.add_from(name, m, self.which[name], expert_offset=self.e0)
         out = {}
         for name, shape in self.full_shapes.items():
             vals, idxs = store.candidate_list(name, device=m.dev)

@@ -48,10 +48,8 @@ class SparseMoELayer:
     def importance(self, x, dy, frac: float, cand_mult: float = 2.0) -> TopKImportanceStore:
         store = TopKImportanceStore(self.shapes, frac, cand_mult)
         self.forward_backward(x, dy)
-        hit = (self.block.expert_cnt > 0).nonzero().reshape(-1)
         for name, p in self.names.items():
-            which = name.rsplit(".", 1)[1]
-            store.add_dense_abs(name, self.block.dense_abs_grad(which), hit)
+            store.add_from(name, self.block, name.rsplit(".", 1)[1])
         return store
 
     def init_selection(self, active: Dict[str, torch.Tensor], lr=1e-4, weight_decay=0.01,

@@ -127,6 +127,28 @@ class TopKImportanceStore:
             self._vals[full_name][eg] = v
             self._idx[full_name][eg] = i
 
+    def add_from(self, full_name: str, block, which: str, expert_offset: int = 0) -> None:
+        """Candidates of one projection straight from a block's backward
+        (``block``: an engine MoEBlock or an ExpertParallelMoE shard whose
+        expert ``e`` is expert ``e + expert_offset`` of the full tensor).  bf16
+        gradients take the fused path (no dense |grad| buffer), others the
+        dense |grad| buffer of :meth:`add_dense_abs`; both keep the experts
+        with routed tokens and resolve equal scores to the lowest index."""
+        if full_name not in self._vals:
+            return
+        numel_e = _numel(self._shapes[full_name][1:])
+        k = min(self._k_of(numel_e), numel_e)
+        res = block.expert_candidates(which, k)
+        if res is None:
+            self.add_dense_abs(full_name, block.dense_abs_grad(which), block.hit_experts(), expert_offset)
+            return
+        vals, idx, experts = res
+        base = expert_offset * numel_e
+        for row, e in enumerate(experts.tolist()):
+            eg = int(e) + expert_offset
+            self._vals[full_name][eg] = vals[row * k:(row + 1) * k]
+            self._idx[full_name][eg] = idx[row * k:(row + 1) * k] + base
+
     def candidates(self, name):
         return dict(self._vals[name]), dict(self._idx[name])
 

@@ -168,9 +168,8 @@ def _capture(experts, blk: MoEBlock, gu: Projection, dn: Projection) -> None:
         dn_s = dn if n_dn in store.compact else _NoOverlay()
         blk.sparse_grads(gu_s, dn_s, store.compact.get(n_gu, empty), store.compact.get(n_dn, empty))
     elif isinstance(store, TopKImportanceStore):
-        hit = (blk.expert_cnt > 0).nonzero().reshape(-1)
         for which in ("gate_up_proj", "down_proj"):
-            store.add_dense_abs(f"{prefix}.{which}", blk.dense_abs_grad(which), hit)
+            store.add_from(f"{prefix}.{which}", blk, which)
     elif isinstance(store, DenseAbsGradStore):
         for which in ("gate_up_proj", "down_proj"):
             store.add_dense_abs(f"{prefix}.{which}", blk.dense_abs_grad(which))
@@ -256,9 +255,8 @@ def _capture_ep(experts, moe, cap) -> None:
     store, prefix = cap
     e0 = moe.rank * moe.El
     if isinstance(store, TopKImportanceStore):
-        hit = (moe.own_cnt > 0).nonzero().reshape(-1)
         for which in ("gate_up_proj", "down_proj"):
-            store.add_dense_abs(f"{prefix}.{which}", moe.dense_abs_grad(which), hit, expert_offset=e0)
+            store.add_from(f"{prefix}.{which}", moe, which, expert_offset=e0)
     elif isinstance(store, DenseAbsGradStore):
         for which in ("gate_up_proj", "down_proj"):
             store.add_dense_abs(f"{prefix}.{which}", moe.dense_abs_grad(which), expert_offset=e0)
