@@ -77,10 +77,12 @@ def test_fused_candidates_equal_dense_path(dev, name):
         n_tie_rows = 0
         for row, e in enumerate(experts.tolist()):
             rv, ri = engine.topk_desc(dense[e].reshape(-1), kk, idx_base=e * numel_e)
+            n_tie_rows += int((rv == rv[-1]).sum() > 1)
+            order = torch.argsort(ri)                    # fused rows are in index order
+            rv, ri = rv[order], ri[order]
             gv, gi = vals[row * kk:(row + 1) * kk], idx[row * kk:(row + 1) * kk]
             assert torch.equal(gi, ri), f"{which} expert {e}: indices differ"
             assert torch.equal(gv, rv), f"{which} expert {e}: values differ"
-            n_tie_rows += int((rv == rv[-1]).sum() > 1)
         if name == "ties_at_zero" and which == "gate_up_proj":
             # the case is built so that some list ends inside a run of equal scores
             assert n_tie_rows > 0
@@ -88,7 +90,8 @@ def test_fused_candidates_equal_dense_path(dev, name):
 
 def test_store_selection_fused_vs_dense(dev):
     """TopKImportanceStore.add_from (fused) and add_dense_abs (dense) give the
-    same per-tensor selection (usaf/moe_loader.py:613-628)."""
+    same per-tensor selection (usaf/moe_loader.py:613-628) and the same
+    per-expert lists from candidates() (descending score, ties by index)."""
     from usaf_b200.moe_loader import TopKImportanceStore
     layer = _layer(dev, **CASES["C2_T512"])
     blk = layer.block
@@ -101,3 +104,8 @@ def test_store_selection_fused_vs_dense(dev):
     sa, sb = a.select(), b.select()
     for name in sa:
         assert torch.equal(sa[name], sb[name]), name
+        va, ia = a.candidates(name)
+        vb, ib = b.candidates(name)
+        assert sorted(va) == sorted(vb)
+        for e in va:
+            assert torch.equal(va[e], vb[e]) and torch.equal(ia[e], ib[e]), (name, e)

@@ -30,7 +30,7 @@ struct SelState {
 constexpr int kTile = 4096;  // elements per block in compaction / sort passes
 
 struct ScratchLayout {
-    size_t state, hist, blk, sort_keys, sort_vals, sort_cnt, total;
+    size_t state, hist, blk, sort_keys, sort_vals, sort_cnt, scan_part, total;
 };
 
 static ScratchLayout layout_for(int64_t n, int64_t k) {
@@ -45,6 +45,7 @@ static ScratchLayout layout_for(int64_t n, int64_t k) {
     L.sort_keys = off; off += al((size_t)k * 2 * sizeof(uint32_t));
     L.sort_vals = off; off += al((size_t)k * 2 * sizeof(int64_t));
     L.sort_cnt = off; off += al((size_t)256 * (nbk + 1) * sizeof(int));
+    L.scan_part = off; off += al((size_t)((256 * (nbk + 1)) / 4096 + 2) * sizeof(int));
     L.total = off;
     return L;
 }
@@ -246,6 +247,77 @@ __global__ void __launch_bounds__(1024) sort_scan(int *cnt, int64_t total) {
     }
 }
 
+// Exclusive scan of the digit counts [256][nb] for large sorts: chunk sums,
+// a one-block scan of those, then each chunk scanned from its offset (a single
+// block walking 256 * nb counts took most of a multi-million-key sort).
+constexpr int kScanChunk = 4096;   // counts per block (4 per thread)
+
+__device__ __forceinline__ int block_excl_scan_1024(int v, int *wt, int &total) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wt[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+        int t = wt[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        wt[lane] = t;
+    }
+    __syncthreads();
+    total = wt[31];
+    return (wid ? wt[wid - 1] : 0) + x - v;
+}
+
+__global__ void __launch_bounds__(1024) scan_chunk_sum(const int *__restrict__ cnt, int64_t total,
+                                                       int *__restrict__ part) {
+    __shared__ int wt[32];
+    const int64_t i0 = (int64_t)blockIdx.x * kScanChunk + threadIdx.x * 4;
+    int v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v += i0 + j < total ? cnt[i0 + j] : 0;
+    int tot;
+    block_excl_scan_1024(v, wt, tot);
+    if (threadIdx.x == 0) part[blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(1024) scan_chunk_apply(int *cnt, int64_t total, const int *__restrict__ part) {
+    __shared__ int wt[32];
+    const int64_t i0 = (int64_t)blockIdx.x * kScanChunk + threadIdx.x * 4;
+    int c[4], v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        c[j] = i0 + j < total ? cnt[i0 + j] : 0;
+        v += c[j];
+    }
+    int tot;
+    int run = block_excl_scan_1024(v, wt, tot) + part[blockIdx.x];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (i0 + j < total) cnt[i0 + j] = run;
+        run += c[j];
+    }
+}
+
+
+static void scan_counts(int *cnt, int64_t total, int *part, cudaStream_t st) {
+    if (total <= kScanChunk) {
+        sort_scan<<<1, 1024, 0, st>>>(cnt, total);
+        return;
+    }
+    const unsigned nch = (unsigned)((total + kScanChunk - 1) / kScanChunk);
+    scan_chunk_sum<<<nch, 1024, 0, st>>>(cnt, total, part);
+    sort_scan<<<1, 1024, 0, st>>>(part, nch);
+    scan_chunk_apply<<<nch, 1024, 0, st>>>(cnt, total, part);
+}
+
 __global__ void __launch_bounds__(256) sort_scatter(const uint32_t *__restrict__ kin,
                                                     const int64_t *__restrict__ vin, int64_t n,
                                                     int shift, const int *__restrict__ cnt,
@@ -362,7 +434,7 @@ extern "C" int usaf_topk_desc(const float *vals, int64_t n, int64_t k, const int
     for (int pass = 0; pass < 4; ++pass) {
         int shift = 8 * pass;
         sort_hist<<<(unsigned)nbk, 256, 0, st>>>(k0, k, shift, cnt, nbk, 0xFFFFFFFFu);
-        sort_scan<<<1, 1024, 0, st>>>(cnt, 256 * nbk);
+        scan_counts(cnt, 256 * nbk, reinterpret_cast<int *>(sc + L.scan_part), st);
         sort_scatter<<<(unsigned)nbk, 256, 0, st>>>(k0, p0, k, shift, cnt, nbk, k1, p1, 0xFFFFFFFFu);
         std::swap(k0, k1);
         std::swap(p0, p1);
@@ -376,7 +448,8 @@ extern "C" int usaf_topk_desc(const float *vals, int64_t n, int64_t k, const int
 extern "C" int64_t usaf_sort_scratch_bytes(int64_t n) {
     if (n < 0) return -1;
     int64_t nb = (n + kTile - 1) / kTile;
-    size_t b = ((size_t)n * 2 * (sizeof(uint32_t) + sizeof(int64_t))) + (size_t)256 * (nb + 1) * sizeof(int) + 1024;
+    size_t b = ((size_t)n * 2 * (sizeof(uint32_t) + sizeof(int64_t))) + (size_t)256 * (nb + 1) * sizeof(int) + 1024 +
+               (size_t)((256 * (nb + 1)) / 4096 + 2) * sizeof(int);
     return (int64_t)b;
 }
 
@@ -396,13 +469,14 @@ extern "C" int usaf_sort_u32(const uint32_t *keys_in, const int64_t *vals_in, in
     int64_t *p1 = p0 + n;
     int *cnt = reinterpret_cast<int *>(p1 + n);
     int64_t nb = (n + kTile - 1) / kTile;
+    int *part = cnt + 256 * (nb + 1);
     cudaMemcpyAsync(k0, keys_in, n * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st);
     cudaMemcpyAsync(p0, vals_in, n * sizeof(int64_t), cudaMemcpyDeviceToDevice, st);
     uint32_t flip = descending ? 0xFFFFFFFFu : 0u;
     for (int pass = 0; pass < 4; ++pass) {
         int shift = 8 * pass;
         sort_hist<<<(unsigned)nb, 256, 0, st>>>(k0, n, shift, cnt, nb, flip);
-        sort_scan<<<1, 1024, 0, st>>>(cnt, 256 * nb);
+        scan_counts(cnt, 256 * nb, part, st);
         sort_scatter<<<(unsigned)nb, 256, 0, st>>>(k0, p0, n, shift, cnt, nb, k1, p1, flip);
         std::swap(k0, k1);
         std::swap(p0, p1);

@@ -52,10 +52,11 @@ def expert_candidates(plan, expert_cnt: torch.Tensor, R: int, C: int, gout: torc
     usaf/moe_loader.py:604-611) for every expert with routed slots, without
     forming the dense gradient: three tensor-core SDDMM passes (exponent
     histogram, histogram inside the threshold bucket, emission) and device
-    sorts.  Returns ``(vals, idx, experts)``: rows of ``k`` scores (descending,
-    ties by ascending flat index) and flat indices ``e*R*C + r*C + c``, one row
-    per entry of ``experts``; or None when the fused path does not cover the
-    shape or dtype (the caller then uses the dense |grad| path)."""
+    sorts.  Returns ``(vals, idx, experts)``: rows of ``k`` scores and flat
+    indices ``e*R*C + r*C + c`` in ascending index order, one row per entry of
+    ``experts`` (each row the set that a descending top-k with equal scores
+    resolved to the lowest index keeps); or None when the fused path does not
+    cover the shape or dtype (the caller then uses the dense |grad| path)."""
     if not _lib.LIB.usaf_importance_supported(R, C, dtc):
         return None
     dev = gout.device
@@ -114,17 +115,15 @@ def expert_candidates(plan, expert_cnt: torch.Tensor, R: int, C: int, gout: torc
              None, None, st)
         call("usaf_importance_take_ties", E, k, ptr(cand_row), ptr(need), ptr(eq_off), ptr(ev), ptr(ei),
              ptr(vals), ptr(idx), st)
-    # rows by descending score, equal scores by ascending index: sort by index,
-    # then stably by (row, descending score)
+    # rows in ascending flat index order (the emission order is a race); the
+    # flat index leads with the expert, so every row stays in place
     keys = torch.empty(n, **i32)
     pos = torch.empty(n, **i64)
     call("usaf_importance_keys", ptr(vals), ptr(idx), None, n, k, 0, None, None, ptr(keys), ptr(pos), st)
     _, perm = sort_u32(keys, pos)
     v1, i1 = torch.empty_like(vals), torch.empty_like(idx)
-    call("usaf_importance_keys", ptr(vals), ptr(idx), ptr(perm), n, k, 1, ptr(v1), ptr(i1), ptr(keys), ptr(pos), st)
-    _, perm = sort_u32(keys, pos)
-    call("usaf_importance_keys", ptr(v1), ptr(i1), ptr(perm), n, k, 2, ptr(vals), ptr(idx), None, None, st)
-    return vals, idx, experts
+    call("usaf_importance_keys", ptr(vals), ptr(idx), ptr(perm), n, k, 2, ptr(v1), ptr(i1), None, None, st)
+    return v1, i1, experts
 
 
 def build_rowptr(rows: torch.Tensor, n_rows: int) -> torch.Tensor:

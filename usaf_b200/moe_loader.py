@@ -150,7 +150,16 @@ class TopKImportanceStore:
             self._idx[full_name][eg] = idx[row * k:(row + 1) * k] + base
 
     def candidates(self, name):
-        return dict(self._vals[name]), dict(self._idx[name])
+        """Per expert (scores, flat indices) in descending score order, equal
+        scores by ascending index (torch.topk's sorted output)."""
+        vals, idxs = {}, {}
+        for e, v in self._vals[name].items():
+            i = self._idx[name][e]
+            if v.numel():
+                vals[e], idxs[e] = engine.topk_desc(v, v.numel(), idx_map=i.to(torch.int64).contiguous())
+            else:
+                vals[e], idxs[e] = v, i
+        return vals, idxs
 
     def select(self, frac: Optional[float] = None) -> Dict[str, torch.Tensor]:
         """Per-tensor top ``min(max(1,int(numel*frac)), n_cand)`` of the
