@@ -602,6 +602,98 @@ def run_c4_sweep(steps: int = 10):
             del blk
 
 
+def run_importance(steps: int = 5, warmup: int = 2):
+    """The importance pass of the C2 layer (one forward/backward, the per-expert
+    top-``2*frac`` candidates of TopKImportanceStore and the per-tensor select;
+    usaf/moe_loader.py:584-631, train.py:540-546), one GPU, CUDA events; one
+    JSON line.  The candidates come from three tensor-core SDDMM passes that
+    never write the gradient (exponent histogram, histogram inside the
+    threshold bucket, emission); the line also times the dense path it
+    replaces (fp32 |dW| buffer + per-expert radix top-k) on the same batch.
+    Roofline: the dense products of a pass (2 P (2I H + H I) FLOP) over the
+    pass's kernel time, against the burst bf16 peak."""
+    from usaf_b200 import _lib
+    import usaf_b200.engine as eng
+    from usaf_b200.moe_loader import TopKImportanceStore
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layer, x, dy = build_layer(dev, 1)
+    torch.cuda.empty_cache()
+    frac = CFG["frac"]
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def fused():
+        store = layer.importance(x, dy, frac)
+        return store.select(frac)
+
+    def dense():
+        layer.forward_backward(x, dy)
+        store = TopKImportanceStore(layer.shapes, frac)
+        for name in layer.names:
+            which = name.rsplit(".", 1)[1]
+            store.add_dense_abs(name, layer.block.dense_abs_grad(which), layer.block.hit_experts())
+        return store.select(frac)
+
+    def timed(fn, n):
+        a, b = ev(), ev()
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(n):
+            out = fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n, out
+
+    for _ in range(warmup):
+        fused()
+        dense()
+    peak_mem0 = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    fused_ms, sel_f = timed(fused, steps)
+    fused_mem = torch.cuda.max_memory_allocated() - peak_mem0
+    torch.cuda.reset_peak_memory_stats()
+    dense_ms, sel_d = timed(dense, max(1, steps // 2))
+    dense_mem = torch.cuda.max_memory_allocated() - peak_mem0
+    same = all(torch.equal(sel_f[n], sel_d[n]) for n in sel_f)
+    # kernel times of the SDDMM passes inside one fused pass
+    orig = _lib.call
+    kev = {}
+
+    def hook(name, *a):
+        if name in ("usaf_importance_hist", "usaf_importance_emit"):
+            e0, e1 = ev(), ev()
+            e0.record()
+            orig(name, *a)
+            e1.record()
+            kev.setdefault(name, []).append((e0, e1))
+        else:
+            orig(name, *a)
+
+    eng.call = hook
+    fused()
+    torch.cuda.synchronize()
+    eng.call = orig
+    hist_ms = sum(a.elapsed_time(b) for a, b in kev["usaf_importance_hist"])
+    emit_ms = sum(a.elapsed_time(b) for a, b in kev["usaf_importance_emit"])
+    P = layer.block.n_pairs_host()
+    flop_pass = 2.0 * P * 3 * CFG["I"] * CFG["H"]
+    _, tc_peak, _, src = peaks()
+    per_pass_ms = (hist_ms + emit_ms) / 3
+    print(json.dumps({"config": "C2", "mode": "importance",
+                      "workload": "importance pass of one Qwen3-30B-A3B MoE layer (T 4096, top-8 candidates "
+                                  "of 1 % per expert, select 0.5 % per tensor), int4 g128, bf16",
+                      "fused_ms": fused_ms, "dense_path_ms": dense_ms,
+                      "speedup_vs_dense_path": dense_ms / fused_ms,
+                      "fused_extra_mem_gb": fused_mem / 1e9, "dense_path_extra_mem_gb": dense_mem / 1e9,
+                      "same_selection_as_dense_path": same,
+                      "sddmm_passes_ms": {"hist_two_passes": hist_ms, "emit": emit_ms},
+                      "roofline": {"bound": "tensor", "achieved": flop_pass / (per_pass_ms * 1e-3) / 1e12,
+                                   "peak": tc_peak, "unit": "TFLOP/s",
+                                   "frac": flop_pass / (per_pass_ms * 1e-3) / 1e12 / tc_peak,
+                                   "flop_per_pass": flop_pass, "peak_source": src},
+                      "pairs": P, "steps": steps, "warmup": warmup, "data": "synthetic"}), flush=True)
+
+
 def run_c5(steps: int = 10, warmup: int = 3):
     """BASELINE configs[4] on one GPU: a Mixtral-8x22B-shaped layer (H=6144,
     E=8, top-2, I=16384, T=4096, int4 g128 experts, bf16): one importance
@@ -774,6 +866,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--c4-sweep", action="store_true",
                     help="time forward and backward separately over the C4 token sweep (1 GPU)")
+    ap.add_argument("--importance", action="store_true",
+                    help="C2 importance pass, fused vs the dense |grad| path (1 GPU)")
     ap.add_argument("--c5", action="store_true",
                     help="Mixtral-8x22B-shaped layer: importance pass + sparse steps (1 GPU)")
     ap.add_argument("--c3", type=int, default=0, metavar="LAYERS",
@@ -785,6 +879,9 @@ def main():
 
     if args.c4_sweep:
         run_c4_sweep()
+        return
+    if args.importance:
+        run_importance()
         return
     if args.c5:
         run_c5()
