@@ -214,3 +214,52 @@ def test_grouped_gemms_write_every_item_repeatably(dev, ci):
             assert torch.equal(a, b), f"{name}: launches differ"
     # the work counters are back at zero for the next launch
     assert int(blk.sched.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("ci", [3, 4], ids=["T512_C2", "T256_skew"])
+def test_in_kernel_dequant_bit_exact(dev, ci):
+    """With one-hot activation rows the grouped GEMMs return single weights:
+    gu[s, r] = W_gu[e][r][c(s)] (forward) and dx[s, c] = W_gu[e][r(s)][c]
+    (transposed backward), each one product 1 * w accumulated in fp32, so
+    the kernels' in-register dequant and overlay patch must equal the
+    reference's bf16(fp16(fp16(q*s)+z)) with trained values
+    (usaf/quantization.py:59-79, usaf/moe_loader.py:241-247) bit for bit."""
+    from usaf_b200 import _lib
+    case = CASES[ci]
+    blk, x, w_r, p = make_case(dev, **case)
+    st = _lib.stream()
+    _lib.call("usaf_router_fwd", _lib.ptr(x), _lib.ptr(w_r), _lib.BF16, case["T"], case["H"],
+              case["E"], case["k"], 1, _lib.ptr(blk.logits), _lib.ptr(blk.probs),
+              _lib.ptr(blk.wsum), _lib.ptr(blk.weights), _lib.ptr(blk.router_ws), _lib.ptr(blk.err), st)
+    _lib.call("usaf_dispatch", blk.plan, _lib.ptr(blk.weights), _lib.ptr(x), _lib.BF16, case["H"],
+              _lib.ptr(blk.x_perm), st)
+    torch.cuda.synchronize()
+    P = blk.n_pairs_host()
+    H, I = case["H"], case["I"]
+    off = blk.expert_off.cpu().tolist()
+    cnt = blk.expert_cnt.cpu().tolist()
+    exp_of = torch.repeat_interleave(torch.arange(case["E"], device=dev),
+                                     torch.tensor(cnt, device=dev), output_size=P)
+    s_idx = torch.arange(P, device=dev)
+    wgu = eff_weight(p["gate_up_proj"]).to(torch.bfloat16)          # [E, 2I, H]
+    # forward: slot s reads input column c(s)
+    c_of = (s_idx * 37) % H
+    blk.x_perm[:P].zero_()
+    blk.x_perm[s_idx, c_of] = 1.0
+    _lib.call("usaf_expert_gate_up_fwd", blk.plan, p["gate_up_proj"].struct(), _lib.ptr(blk.x_perm),
+              _lib.BF16, _lib.ptr(blk.gu), _lib.ptr(blk.h), st)
+    # transposed backward: slot s reads weight row r(s)
+    r_of = (s_idx * 29) % (2 * I)
+    blk.dgu[:P].zero_()
+    blk.dgu[s_idx, r_of] = 1.0
+    _lib.call("usaf_expert_gate_up_bwd", blk.plan, p["gate_up_proj"].struct(), _lib.ptr(blk.dgu),
+              _lib.BF16, _lib.ptr(blk.dx_seg), st)
+    torch.cuda.synchronize()
+    blk.check()
+    want_fwd = wgu[exp_of, :, c_of]                                   # [P, 2I]
+    assert torch.equal(blk.gu[:P], want_fwd), \
+        f"forward: {int((blk.gu[:P] != want_fwd).sum())} weights differ"
+    want_bwd = wgu[exp_of, r_of, :]                                   # [P, H]
+    assert torch.equal(blk.dx_seg[:P], want_bwd), \
+        f"transposed: {int((blk.dx_seg[:P] != want_bwd).sum())} weights differ"
+    assert off[-1] == P
