@@ -427,9 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int pj = hit ? (rel >> 1) : 0xFF;
                 const uint32_t qb0 = __bfloat16_as_ushort(__float2bfloat16_rn(qv0));
                 const uint32_t m2 = qb0 | (qb0 << 16);
-                const uint32_t sel = (rel & 1) ? 0x5410u : 0x3254u;
+                const uint32_t hm = (rel & 1) ? 0xFFFF0000u : 0x0000FFFFu;
                 uint32_t r[16];
-                dequant16<TRANS>(A, Z.x | (Z.y << 16), szr, pj, m2, sel, r);
+                dequant16<TRANS>(A, Z.x | (Z.y << 16), szr, pj, m2, hm, r);
                 if (kb + 3 < nk) USAF_LOAD(kb + 3, A, Z);   // refill the consumed slot
                 if (hit) {
                     // advance the queue; more coordinates in this block take the slow path

@@ -25,10 +25,11 @@ static __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity
 // then bf16.  SCALE_PER_ROW: pair i has its own (scale, zero) per element
 // (transposed weights); otherwise one (scale, zero) for the whole block.
 // A pending trained coordinate at pair pj is blended in after the bf16
-// conversion (sel picks the half).
+// conversion: m2 holds its bf16 value in both halves, hm selects the half.
+// One compare and one predicated bit select per pair.
 template <bool SCALE_PER_ROW>
 static __device__ __forceinline__ void dequant16(uint4 codes, uint32_t szw, const uint32_t *szr, int pj,
-                                          uint32_t m2, uint32_t sel, uint32_t (&r)[16]) {
+                                          uint32_t m2, uint32_t hm, uint32_t (&r)[16]) {
     const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
     const __half2 magic = __half2half2(__ushort_as_half((unsigned short)0x6400));
     __half2 s2 = __half2half2(__ushort_as_half((unsigned short)(szw & 0xFFFF)));
@@ -47,22 +48,25 @@ static __device__ __forceinline__ void dequant16(uint4 codes, uint32_t szw, cons
         float2 f = __half22float2(v);
         __nv_bfloat162 bb = __floats2bfloat162_rn(f.x, f.y);
         uint32_t rv = *reinterpret_cast<uint32_t *>(&bb);
-        r[i] = (i == pj) ? __byte_perm(rv, m2, sel) : rv;
+        asm("{\n .reg .pred p;\n setp.eq.s32 p, %1, %2;\n @p lop3.b32 %0, %0, %3, %4, 0xD8;\n}\n"
+            : "+r"(rv)
+            : "r"(pj), "r"(i), "r"(m2), "r"(hm));
+        r[i] = rv;
     }
 }
 
-// slow path for a second trained coordinate in the same 32-wide block:
-// predicated select per register keeps r[] in registers
+// slow path for a second trained coordinate in the same 32-wide block: one
+// compare and one predicated bit select (lop3 "c ? b : a") per register keeps
+// r[] in registers
 static __device__ __forceinline__ void patch_elem16(uint32_t (&r)[16], int c, uint32_t vb) {
     const uint32_t pi = (uint32_t)c >> 1;
-    const bool hi = c & 1;
+    const uint32_t v2 = vb | (vb << 16);
+    const uint32_t hm = (c & 1) ? 0xFFFF0000u : 0x0000FFFFu;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const uint32_t cand = hi ? ((r[i] & 0xFFFFu) | (vb << 16)) : ((r[i] & 0xFFFF0000u) | vb);
-        asm volatile("{\n .reg .pred p;\n setp.eq.u32 p, %1, %2;\n selp.b32 %0, %3, %0, p;\n}\n"
-                     : "+r"(r[i])
-                     : "r"(pi), "r"((uint32_t)i), "r"(cand));
-    }
+    for (int i = 0; i < 16; ++i)
+        asm("{\n .reg .pred p;\n setp.eq.u32 p, %1, %2;\n @p lop3.b32 %0, %0, %3, %4, 0xD8;\n}\n"
+            : "+r"(r[i])
+            : "r"(pi), "r"((uint32_t)i), "r"(v2), "r"(hm));
 }
 
 // packed fp32 pairs (sm_100 f32x2 arithmetic, round to nearest even)
