@@ -87,8 +87,9 @@ typedef struct {
     const float   *valT;      /* [n_ov]   effective value of each CSC entry        */
     /* copies for the tensor-core GEMMs, codes in the usaf_int4_repack order:
      * qP [E*R*C/2] row-major (forward), qT [E*C*R/2] column-major (backward,
-     * usaf_int4_transpose), szT [E*(C/group_size)*R] uint32 (scale | zero << 16)
-     * per (column group, row) */
+     * usaf_int4_transpose), szT [E*(C/group_size)*R] uint32: per (column
+     * group, pair of rows 2p, 2p+1) the words scale[2p] | scale[2p+1] << 16
+     * and zero[2p] | zero[2p+1] << 16 */
     const int8_t   *qT;
     const uint32_t *szT;
     const int8_t   *qP;

@@ -22,8 +22,9 @@ static __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity
 // Dequantize 32 elements (16 pairs) from 4 code words in the repacked
 // order: pair i = nibbles (i%4, i%4+4) of word i/4.  fp16(fp16(q*s)+z) per
 // element (separately rounded multiply and add, the reference's rounding),
-// then bf16.  SCALE_PER_ROW: pair i has its own (scale, zero) per element
-// (transposed weights); otherwise one (scale, zero) for the whole block.
+// then bf16.  SCALE_PER_ROW: pair i has its own scales and zeros, szr[2i] and
+// szr[2i+1] as half2 (transposed weights); otherwise one (scale, zero) for the
+// whole block.
 // A pending trained coordinate at pair pj is blended in after the bf16
 // conversion: m2 holds its bf16 value in both halves, hm selects the half.
 // One compare and one predicated bit select per pair.
@@ -39,8 +40,8 @@ static __device__ __forceinline__ void dequant16(uint4 codes, uint32_t szw, cons
         uint32_t u = ((w[i >> 2] >> (4 * (i & 3))) & 0x000F000Fu) | 0x64006400u;
         __half2 c = __hsub2(*reinterpret_cast<__half2 *>(&u), magic);
         if (SCALE_PER_ROW) {
-            uint32_t wa = szr[2 * i], wb = szr[2 * i + 1];
-            uint32_t su = __byte_perm(wa, wb, 0x5410), zu = __byte_perm(wa, wb, 0x7632);
+            // the pair's scales and zeros arrive packed as half2 words
+            uint32_t su = szr[2 * i], zu = szr[2 * i + 1];
             s2 = *reinterpret_cast<__half2 *>(&su);
             z2 = *reinterpret_cast<__half2 *>(&zu);
         }

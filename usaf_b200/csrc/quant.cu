@@ -209,18 +209,22 @@ __global__ void int4_transpose_codes(const uint8_t *__restrict__ q, int E, int R
         qT[i] = out;
     }
 }
-// szT[(e*(C/gs) + cb)*R + r] = s[(e*R + r)*(C/gs) + cb] | z[...] << 16
+// Per (expert, column group), two words per pair of rows 2p, 2p+1:
+// szT[(e*(C/gs) + cb)*R + 2p]     = s[row 2p] | s[row 2p+1] << 16,
+// szT[(e*(C/gs) + cb)*R + 2p + 1] = z[row 2p] | z[row 2p+1] << 16
+// (the half2 scale and zero operands of a dequantized element pair as they are)
 __global__ void int4_transpose_scales(const uint16_t *__restrict__ s, const uint16_t *__restrict__ z,
                                       int E, int R, int C, int gs, uint32_t *__restrict__ szT) {
     const int ncb = C / gs;
     const int64_t total = (int64_t)E * ncb * R;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        int64_t r = i % R;
-        int64_t ecb = i / R;
-        int64_t cb = ecb % ncb, e = ecb / ncb;
-        int64_t src = (e * R + r) * ncb + cb;
-        szT[i] = (uint32_t)s[src] | ((uint32_t)z[src] << 16);
+        const int64_t r = i % R;
+        const int64_t ecb = i / R;
+        const int64_t cb = ecb % ncb, e = ecb / ncb;
+        const int64_t r0 = r & ~(int64_t)1;
+        const uint16_t *src = (r & 1) ? z : s;
+        szT[i] = (uint32_t)src[(e * R + r0) * ncb + cb] | ((uint32_t)src[(e * R + r0 + 1) * ncb + cb] << 16);
     }
 }
 }  // namespace usaf
