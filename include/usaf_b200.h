@@ -103,6 +103,12 @@ typedef struct {
      * (usaf_build_ov_cbptr).  The tensor-core usaf_sparse_dw needs it with
      * ov_mask; NULL selects the SIMT gradient kernel. */
     const int32_t *ov_cbptr;
+    /* [E] or NULL: the largest number of overlay coordinates in one storage
+     * row (ov_emax) / storage column (ov_emaxT) of each expert.  The grouped
+     * GEMMs order their work by it besides the token count: a heavily
+     * trained row or column slows the whole item it belongs to. */
+    const int32_t *ov_emax;
+    const int32_t *ov_emaxT;
 } usaf_qweight;
 
 /* ---- int4 format ---------------------------------------------------------

@@ -33,7 +33,7 @@ class QWeight(C.Structure):
                 ("q", P), ("s", P), ("z", P), ("n_ov", I32),
                 ("row_ptr", P), ("col", P), ("val", P),
                 ("colT_ptr", P), ("rowT", P), ("valT", P), ("qT", P), ("szT", P), ("qP", P),
-                ("ov_mask", P), ("ov_cbptr", P)]
+                ("ov_mask", P), ("ov_cbptr", P), ("ov_emax", P), ("ov_emaxT", P)]
 
 
 # name -> (restype, argtypes)

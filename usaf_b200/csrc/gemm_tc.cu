@@ -197,14 +197,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // it), so the placement is a scan, not shared-memory atomics.
     const bool sorted = n_tiles <= kMaxOrder;
     if (sorted) {
-        constexpr int kNB = kMaxTok / 16 + 1;
+        // bucket = token count / 16, plus the trained coordinates per k-block of the
+        // expert's most trained row (column, backward): a row whose coordinates the
+        // producer lane walks one by one can make an item take twice as long
+        constexpr int kHeavyMax = 40;
+        constexpr int kNB = kMaxTok / 16 + kHeavyMax + 1;
+        const int32_t *emax = w.n_ov ? (TRANS ? w.ov_emaxT : w.ov_emax) : nullptr;
         __shared__ unsigned char bkt[1024];
         __shared__ int bcnt[kNB], bpos[kNB];
         if (tid < kNB) bcnt[tid] = 0;
         __syncthreads();
         for (int e_ = tid; e_ < E; e_ += kThreads) {
             const int ntt = tile_off[e_ + 1] - tile_off[e_];
-            bkt[e_] = ntt ? (unsigned char)tile_bucket(cnts[e_], ntt) : (unsigned char)255;
+            const int heavy = emax ? min(emax[e_] / nk, kHeavyMax) : 0;
+            bkt[e_] = ntt ? (unsigned char)(tile_bucket(cnts[e_], ntt) + heavy) : (unsigned char)255;
             if (ntt) atomicAdd(&bcnt[bkt[e_]], ntt);   // integer sums: the same in every CTA
         }
         __syncthreads();

@@ -223,6 +223,7 @@ class Projection:
         self.csr_identity = False
         self.scratch = None
         self.ov_mask = self.ov_cbptr = None
+        self.ov_emax = self.ov_emaxT = None
         self.qT = self.szT = self.qP = None
         if dtype == torch.bfloat16 and R % 8 == 0 and Cc % 8 == 0:
             # dequant-ordered copies for the tensor-core GEMMs (built once):
@@ -305,6 +306,9 @@ class Projection:
             self.ov_cbptr = torch.empty(E * R * ((Cc + 255) // 256) * 2, dtype=torch.int32, device=dev)
             call("usaf_build_ov_cbptr", ptr(self.row_ptr), ptr(self.col), E, R, Cc, ptr(self.ov_cbptr),
                  stream())
+        # per expert: the most trained storage row and column (work order of the GEMMs)
+        self.ov_emax = (self.row_ptr[2::2] - self.row_ptr[:-1:2]).view(E, R).amax(1).to(torch.int32)
+        self.ov_emaxT = (self.colT_ptr[2::2] - self.colT_ptr[:-1:2]).view(E, Cc).amax(1).to(torch.int32)
         self.val = torch.empty(n, dtype=torch.float32, device=dev)
         self.valT = torch.empty(n, dtype=torch.float32, device=dev)
         self.update_overlay_values(master)
@@ -328,6 +332,8 @@ class Projection:
             st.qT, st.szT, st.qP = ptr(self.qT), ptr(self.szT), ptr(self.qP)
             st.ov_mask = ptr(self.ov_mask) if (self.n_ov and self.ov_mask is not None) else None
             st.ov_cbptr = ptr(self.ov_cbptr) if (self.n_ov and self.ov_cbptr is not None) else None
+            if self.n_ov:
+                st.ov_emax, st.ov_emaxT = ptr(self.ov_emax), ptr(self.ov_emaxT)
             self._struct = st
         return self._struct
 
