@@ -314,15 +314,14 @@ int usaf_expert_dense_dw(const usaf_route_plan *plan, int32_t R, int32_t C, cons
  *   the need[e] lowest-index ties to each row;
  *   usaf_importance_keys mode 0 + usaf_sort_u32, then mode 1 + usaf_sort_u32,
  *   then mode 2: rows ordered by descending value, ties by ascending index.
- * part / part_slot: fp32 partial sums [n * R * C] of the experts with more
- * than usaf_importance_chunk_slots() slots (part_slot[e] their slot, -1 for
- * the rest; may be NULL when no expert has that many).  cand_row[e] < 0 or
- * thr[e] < 0 leaves expert e out.  Flat indices are e*R*C + r*C + c. */
+ * cand_row[e] < 0 or thr[e] < 0 leaves expert e out.  Flat indices are
+ * e*R*C + r*C + c.  usaf_importance_chunk_slots(): slots of one SDDMM chunk
+ * (an expert with more is summed over several in the accumulator). */
 int32_t usaf_importance_chunk_slots(void);
 int usaf_importance_supported(int32_t R, int32_t C, int32_t dtype);
 int usaf_importance_hist(const usaf_route_plan *plan, int32_t R, int32_t C, const void *gout,
                          const void *gin, int32_t dtype, int32_t level, const int32_t *pval,
-                         uint32_t *hist, float *part, const int32_t *part_slot, void *stream);
+                         uint32_t *hist, void *stream);
 int usaf_importance_pick(const uint32_t *hist, int32_t E, int64_t k, const int32_t *expert_cnt,
                          int32_t level, int32_t *pval, int64_t *need, int32_t *thr, int64_t *n_eq,
                          void *stream);
@@ -330,7 +329,7 @@ int usaf_importance_emit(const usaf_route_plan *plan, int32_t R, int32_t C, cons
                          const void *gin, int32_t dtype, const int32_t *thr, int64_t k,
                          const int32_t *cand_row, int32_t *n_gt, int32_t *n_eq, float *cand_val,
                          int64_t *cand_idx, const int64_t *eq_off, float *eq_val, int64_t *eq_idx,
-                         float *part, const int32_t *part_slot, void *stream);
+                         void *stream);
 int usaf_importance_take_ties(int32_t E, int64_t k, const int32_t *cand_row, const int64_t *need,
                               const int64_t *eq_off, const float *eq_val, const int64_t *eq_idx,
                               float *cand_val, int64_t *cand_idx, void *stream);

@@ -54,6 +54,7 @@ CASES = {
     "C2_T512": dict(T=512, H=2048, E=128, k=8, I=768),
     "C2_T4096_zipf": dict(T=4096, H=2048, E=128, k=8, I=768, zipf=1.2),   # experts > 320 slots
     "ties_at_zero": dict(T=256, H=512, E=16, k=4, I=256, zero_cols=2),     # threshold on zeros
+    "tiny_C128": dict(T=64, H=256, E=8, k=2, I=128),                        # 128-column tiles (down)
 }
 
 

@@ -66,10 +66,10 @@ _SIGS = {
     "usaf_kth_largest": (I32, [P, I64, I64, P, P, P]),
     "usaf_importance_chunk_slots": (I32, []),
     "usaf_importance_supported": (I32, [I32, I32, I32]),
-    "usaf_importance_hist": (I32, [C.POINTER(RoutePlan), I32, I32, P, P, I32, I32, P, P, P, P, P]),
+    "usaf_importance_hist": (I32, [C.POINTER(RoutePlan), I32, I32, P, P, I32, I32, P, P, P]),
     "usaf_importance_pick": (I32, [P, I32, I64, P, I32, P, P, P, P, P]),
     "usaf_importance_emit": (I32, [C.POINTER(RoutePlan), I32, I32, P, P, I32, P, I64, P, P, P, P, P, P, P, P,
-                                   P, P, P]),
+                                   P]),
     "usaf_importance_take_ties": (I32, [I32, I64, P, P, P, P, P, P, P, P]),
     "usaf_importance_keys": (I32, [P, P, P, I64, I64, I32, P, P, P, P, P]),
     "usaf_sort_scratch_bytes": (I64, [I64]),

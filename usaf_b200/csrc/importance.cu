@@ -17,19 +17,19 @@
 //           indices appended to each candidate list (ties resolve to the
 //           lowest flat index, as usaf_topk_desc does);
 //   order   each list sorted by descending value, ties by ascending index.
-// An expert whose slots span several SDDMM chunks keeps its fp32 partial sums
-// in a caller scratch between chunks (usaf_importance_chunk_slots()).
+// An expert whose slots span several SDDMM chunks is summed chunk after chunk
+// in TMEM (usaf_importance_chunk_slots() slots per chunk).
 #include "common.cuh"
 
 namespace usaf {
 
 int sddmm_tc_key_hist(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
                       const __nv_bfloat16 *gin, int shift, int pmask, const int32_t *pval,
-                      unsigned int *hist, float *part, const int32_t *part_slot, cudaStream_t st);
+                      unsigned int *hist, cudaStream_t st);
 int sddmm_tc_key_emit(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
                       const __nv_bfloat16 *gin, const int32_t *thr, int64_t k, const int32_t *cand_row,
                       int32_t *n_gt, int32_t *n_eq, float *gt_val, int64_t *gt_idx, const int64_t *eq_off,
-                      float *eq_val, int64_t *eq_idx, float *part, const int32_t *part_slot, cudaStream_t st);
+                      float *eq_val, int64_t *eq_idx, cudaStream_t st);
 int sddmm_tc_chunk_slots();
 bool sddmm_tc_supported(int R, int C);
 
@@ -135,14 +135,14 @@ extern "C" int usaf_importance_supported(int32_t R, int32_t C, int32_t dtype) {
 
 extern "C" int usaf_importance_hist(const usaf_route_plan *plan, int32_t R, int32_t C, const void *gout,
                                     const void *gin, int32_t dtype, int32_t level, const int32_t *pval,
-                                    uint32_t *hist, float *part, const int32_t *part_slot, void *stream) {
+                                    uint32_t *hist, void *stream) {
     USAF_REQUIRE(plan && gout && gin && hist && R >= 1 && C >= 1 && (level == 1 || (level == 2 && pval)));
     if (!usaf_importance_supported(R, C, dtype)) return USAF_EUNSUPPORTED;
     // level 1: every key, binned by its exponent; level 2: the keys of the chosen
     // exponent bucket, binned by their low 8 bits
     const int shift = level == 1 ? 7 : 0, pmask = level == 1 ? 0 : 0x7F80;
     return sddmm_tc_key_hist(plan, R, C, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin, shift, pmask,
-                             level == 1 ? nullptr : pval, hist, part, part_slot, as_stream(stream));
+                             level == 1 ? nullptr : pval, hist, as_stream(stream));
 }
 
 extern "C" int usaf_importance_pick(const uint32_t *hist, int32_t E, int64_t k, const int32_t *expert_cnt,
@@ -159,13 +159,12 @@ extern "C" int usaf_importance_emit(const usaf_route_plan *plan, int32_t R, int3
                                     const void *gin, int32_t dtype, const int32_t *thr, int64_t k,
                                     const int32_t *cand_row, int32_t *n_gt, int32_t *n_eq, float *cand_val,
                                     int64_t *cand_idx, const int64_t *eq_off, float *eq_val, int64_t *eq_idx,
-                                    float *part, const int32_t *part_slot, void *stream) {
+                                    void *stream) {
     USAF_REQUIRE(plan && gout && gin && thr && k >= 1 && cand_row && n_gt && n_eq && cand_val && cand_idx &&
                  eq_off && R >= 1 && C >= 1);
     if (!usaf_importance_supported(R, C, dtype)) return USAF_EUNSUPPORTED;
     return sddmm_tc_key_emit(plan, R, C, (const __nv_bfloat16 *)gout, (const __nv_bfloat16 *)gin, thr, k, cand_row,
-                             n_gt, n_eq, cand_val, cand_idx, eq_off, eq_val, eq_idx, part, part_slot,
-                             as_stream(stream));
+                             n_gt, n_eq, cand_val, cand_idx, eq_off, eq_val, eq_idx, as_stream(stream));
 }
 
 extern "C" int usaf_importance_take_ties(int32_t E, int64_t k, const int32_t *cand_row, const int64_t *need,

@@ -24,9 +24,9 @@
 //   EPI_EMIT     : the same keys against a threshold per expert: every
 //                  coordinate above it goes to the expert's candidate list,
 //                  every one equal to it to the expert's tie list.
-//   Experts whose slots span several chunks keep their partial sums in
-//   fp32 (in `out` for EPI_DENSE_ABS, in a caller scratch for the
-//   importance modes).
+//   An expert whose slots exceed one resident chunk is summed chunk after
+//   chunk into the same TMEM accumulator (its gin chunks reloaded for every
+//   row block), so no partial sums leave the SM in any mode.
 //
 // Tile = 128 storage rows x 256 columns (MMA M x N), K = the expert's slots in
 // blocks of 64.  Both operands reach shared memory as TMA boxes of 64 slots x
@@ -370,38 +370,11 @@ struct ImpArgs {
     const int64_t *eq_off;       // EMIT: [E] start of e's tie list
     float *eq_val;
     int64_t *eq_idx;
-    float *part;                 // fp32 partial sums of experts that take several chunks
-    const int32_t *part_slot;    // [E] their slot in `part`, -1 for the others
 };
 
 // 15-bit order key of |bf16(v)|: exponent and mantissa bits of the rounded value
 __device__ __forceinline__ int abs_key(float v) {
     return (int)((__float_as_uint(round_bf16(v)) >> 16) & 0x7FFFu);
-}
-
-// the final value of one 32-column chunk of a row (partials of earlier chunks
-// added), or nothing when this chunk is not the expert's last
-__device__ __forceinline__ bool chunk_final(uint32_t (&v)[32], float *part_row, int mode) {
-    if (mode == PART_ALL) return true;
-    float4 *o4 = reinterpret_cast<float4 *>(part_row);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float4 a = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-        if (mode != PART_FIRST) {
-            const float4 b = o4[i];
-            a = make_float4(__fadd_rn(b.x, a.x), __fadd_rn(b.y, a.y), __fadd_rn(b.z, a.z), __fadd_rn(b.w, a.w));
-        }
-        if (mode == PART_LAST) {
-            v[4 * i] = __float_as_uint(a.x);
-            v[4 * i + 1] = __float_as_uint(a.y);
-            v[4 * i + 2] = __float_as_uint(a.z);
-            v[4 * i + 3] = __float_as_uint(a.w);
-        } else {
-            o4[i] = a;
-        }
-    }
-    return mode == PART_LAST;
 }
 
 __device__ __forceinline__ void hist_chunk(const uint32_t (&v)[32], unsigned int *h, int shift, int pmask, int pv) {
@@ -527,26 +500,32 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const int c0 = s.cb * kSN;
                 const int nb = min(4, (C - c0) / 64);
                 const bool ragged = ch.nk > 0 && ((cnt - (ch.nk - 1) * kSK) & 15) != 0;
-                for (int kc = 0; kc < ch.n && ok; ++kc) {
-                    const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
-                    // the previous chunk's MMAs have read the resident block
-                    if (!mbar_wait(&S.b_empty, (bc & 1) ^ 1, abort_flag, err)) {
-                        ok = false;
-                        break;
-                    }
-                    // every b_full barrier completes once per chunk, so their phases stay
-                    // in step with the chunk count: the ones this chunk leaves unused get
-                    // a plain arrive, before any load is issued (a waiter that saw
-                    // b_full[0] complete knows they have completed too)
-                    for (int k = kb1 - kb0; k < kBMaxKb; ++k) mbar_arrive(&S.b_full[k]);
-                    for (int k = 0; k < kb1 - kb0; ++k) {
-                        mbar_arrive_expect_tx(&S.b_full[k], (uint32_t)(nb * kBox));
-                        const int y = row0 + (kb0 + k) * kSK;
-                        for (int j = 0; j < nb; ++j)
-                            tma_load_2d(b_res + (size_t)k * kBKb + j * kBox, &tm_in, &S.b_full[k], c0 + 64 * j, y);
-                    }
-                    ++bc;
-                    for (int rb = s.rb0; rb < s.rb1 && ok; ++rb) {
+                // an expert within one chunk keeps its gin block resident for the whole run;
+                // a larger one reloads chunk after chunk for every row block, and the row
+                // block's accumulator sums all of them (no partial sums leave the SM)
+                const bool multi = ch.n > 1;
+                for (int rb = s.rb0; rb < s.rb1 && ok && ch.n; ++rb) {
+                    for (int kc = 0; kc < ch.n && ok; ++kc) {
+                        const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
+                        if (multi || rb == s.rb0) {
+                            // the previous chunk's MMAs have read the resident block
+                            if (!mbar_wait(&S.b_empty, (bc & 1) ^ 1, abort_flag, err)) {
+                                ok = false;
+                                break;
+                            }
+                            // every b_full barrier completes once per chunk load, so their
+                            // phases stay in step with the load count: the ones this chunk
+                            // leaves unused get a plain arrive, before any load is issued (a
+                            // waiter that saw b_full[0] complete knows they have completed too)
+                            for (int k = kb1 - kb0; k < kBMaxKb; ++k) mbar_arrive(&S.b_full[k]);
+                            for (int k = 0; k < kb1 - kb0; ++k) {
+                                mbar_arrive_expect_tx(&S.b_full[k], (uint32_t)(nb * kBox));
+                                const int y = row0 + (kb0 + k) * kSK;
+                                for (int j = 0; j < nb; ++j)
+                                    tma_load_2d(b_res + (size_t)k * kBKb + j * kBox, &tm_in, &S.b_full[k], c0 + 64 * j, y);
+                            }
+                            ++bc;
+                        }
                         for (int kb = kb0; kb < kb1; ++kb, ++ga) {
                             const int st = ga % AST;
                             if (!mbar_wait(&S.a_empty[st], ((ga / AST) & 1) ^ 1, abort_flag, err)) {
@@ -589,16 +568,19 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const int nb = min(4, (C - s.cb * kSN) / 64);
                 const uint32_t idesc = idesc_mn(kSM, nb * 64);
                 const bool ragged = ch.nk > 0 && ((cnt - (ch.nk - 1) * kSK) & 15) != 0;
-                for (int kc = 0; kc < ch.n && ok; ++kc) {
-                    const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
-                    for (int rb = s.rb0; rb < s.rb1 && ok; ++rb, ++it) {
-                        const int buf = it & 1;
-                        if (!(ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err))) break;
-                        tc_fence_after();
+                const bool multi = ch.n > 1;
+                // (an expert without slots has no tiles: nothing to issue or drain)
+                for (int rb = s.rb0; rb < s.rb1 && ok && ch.n; ++rb, ++it) {
+                    const int buf = it & 1;
+                    if (!(ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err))) break;
+                    tc_fence_after();
+                    for (int kc = 0; kc < ch.n && ok; ++kc) {
+                        const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
+                        const bool new_b = multi || rb == s.rb0;
                         for (int kb = kb0; kb < kb1; ++kb, ++ga) {
                             const int kbl = kb - kb0, st = ga % AST;
-                            // first tile of the chunk: the resident block is in place
-                            if (rb == s.rb0 && !(ok = mbar_wait(&S.b_ready[kbl], bc & 1, abort_flag, err))) break;
+                            // first use of a loaded chunk: the resident block is in place
+                            if (new_b && !(ok = mbar_wait(&S.b_ready[kbl], bc & 1, abort_flag, err))) break;
                             // a stage that needs no zeroing is taken straight from the TMA
                             // barrier; the expert's ragged last k-block comes through the
                             // forwarder
@@ -612,23 +594,29 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             const uint64_t da = dA0 + (uint64_t)((st * kAStage) >> 4);
                             const uint64_t db = dB0 + (uint64_t)((kbl * kBKb) >> 4);
                             const uint32_t dt = tbase + buf * kSN;
+                            // the row block's accumulator sums every chunk of the expert
+                            const bool first = kc == 0 && kb == kb0;
                             if (kb < ch.nk - 1) {   // a full k-block: four MMAs
 #pragma unroll
                                 for (int kk = 0; kk < 4; ++kk)
-                                    mma_ss(dt, da + kk * (2048 >> 4), db + kk * (2048 >> 4), idesc, (kb > kb0 || kk > 0));
+                                    mma_ss(dt, da + kk * (2048 >> 4), db + kk * (2048 >> 4), idesc, !(first && kk == 0));
                             } else {
                                 const int nks = (min(kSK, cnt - kb * kSK) + 15) / 16;
                                 for (int kk = 0; kk < nks; ++kk)
-                                    mma_ss(dt, da + kk * (2048 >> 4), db + kk * (2048 >> 4), idesc, (kb > kb0 || kk > 0));
+                                    mma_ss(dt, da + kk * (2048 >> 4), db + kk * (2048 >> 4), idesc, !(first && kk == 0));
                             }
                             mma_commit(&S.a_empty[st]);
                         }
                         if (!ok) break;
-                        mma_commit(&S.acc_full[buf]);
+                        // the loaded chunk is done with: every chunk of a large expert, the
+                        // run's single chunk after its last row block
+                        if (multi || rb == s.rb1 - 1) {
+                            mma_commit(&S.b_empty);
+                            ++bc;
+                        }
                     }
                     if (!ok) break;
-                    mma_commit(&S.b_empty);
-                    ++bc;
+                    mma_commit(&S.acc_full[buf]);
                 }
             }
             // every MMA this CTA issued has completed before TMEM is released
@@ -651,13 +639,14 @@ __global__ void __launch_bounds__(kSThreads, 1)
             // belongs to the next expert and is zeroed in both operands
             const int rem = cnt - (ch.nk - 1) * kSK;
             const bool ragged = ch.nk > 0 && (rem & 15) != 0;
-            for (int kc = 0; kc < ch.n && ok; ++kc) {
-                const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
-                for (int rb = s.rb0; rb < s.rb1 && ok; ++rb) {
+            const bool multi = ch.n > 1;
+            for (int rb = s.rb0; rb < s.rb1 && ok && ch.n; ++rb) {
+                for (int kc = 0; kc < ch.n && ok; ++kc) {
+                    const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
                     for (int kb = kb0; kb < kb1; ++kb, ++ga) {
                         const int kbl = kb - kb0, st = ga % AST;
                         const bool tail = ragged && kb == ch.nk - 1;
-                        if (rb == s.rb0) {
+                        if (multi || rb == s.rb0) {
                             if (!(ok = warp_wait(&S.b_full[kbl], bc & 1, abort_flag, err))) break;
                             if (tail) {
                                 zero_tail(b_res + (size_t)kbl * kBKb, nb, rem, lane);
@@ -687,8 +676,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             tail_par ^= 1u << st;
                         }
                     }
+                    if (multi || rb == s.rb1 - 1) ++bc;
                 }
-                ++bc;
             }
         }
     } else {
@@ -717,10 +706,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
             const int nch = min(8, (C - c0) / 32);
             const int j0 = min(nch, 2 * slice), j1 = min(nch, 2 * slice + 2);
             // importance: an expert without slots has no gradient hook in the reference
-            // (and a threshold below zero means the caller left the expert out)
-            if (EPI >= EPI_HIST && (cnt == 0 || (EPI == EPI_EMIT && ia.thr[s.e] < 0) ||
-                                    (EPI == EPI_HIST && ia.pmask && ia.pval[s.e] < 0)))
-                continue;
+            // (it has no tiles either); a threshold below zero means the caller left
+            // the expert out: its tiles are drained without counting or emitting
+            if (EPI >= EPI_HIST && cnt == 0) continue;
+            const bool imp_skip = (EPI == EPI_EMIT && ia.thr[s.e] < 0) ||
+                                  (EPI == EPI_HIST && ia.pmask && ia.pval[s.e] < 0);
             if (cnt == 0) {
                 // no slots: the gradient is exactly zero
                 for (int rb = s.rb0; rb < s.rb1; ++rb) {
@@ -738,8 +728,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 }
                 continue;
             }
-            for (int kc = 0; kc < ch.n && ok; ++kc) {
-                const int mode = ch.n == 1 ? PART_ALL : kc == 0 ? PART_FIRST : kc == ch.n - 1 ? PART_LAST : PART_MID;
+            {
+                // one drain per row block: its accumulator holds the sum over every chunk
+                const int mode = PART_ALL;
                 // this row's selection in the warp's two chunks and its first CSR
                 // positions in the two halves: loaded one row block ahead, so the
                 // loads' latency hides behind a whole tile
@@ -769,22 +760,18 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         tmem_ld_32x32b_x32(tb + 32 * j0 + 32, va);
                         tmem_wait_ld();
                         drain_sparse(va, mw.y, p1, mode, out);
-                    } else if (j0 < j1 && EPI >= EPI_HIST) {
+                    } else if (j0 < j1 && EPI >= EPI_HIST && !imp_skip) {
                         const int64_t lrow = (int64_t)rb * kSM + rr;   // row inside the expert
-                        float *prow = mode == PART_ALL ? nullptr
-                                    : ia.part + ((int64_t)ia.part_slot[s.e] * R + lrow) * C + c0 + 32 * j0;
                         const int64_t flat0 = ((int64_t)s.e * R + lrow) * C + c0 + 32 * j0;
 #pragma unroll 1
                         for (int h = 0; h < 2; ++h) {
                             uint32_t va[32];
                             tmem_ld_32x32b_x32(tb + 32 * (j0 + h), va);
                             tmem_wait_ld();
-                            if (chunk_final(va, prow + 32 * h, mode)) {
-                                if (EPI == EPI_HIST) hist_chunk(va, hw, ia.shift, ia.pmask, ia.pmask ? ia.pval[s.e] : 0);
-                                else emit_chunk(va, s.e, flat0 + 32 * h, ia.thr[s.e], ia, lane);
-                            }
+                            if (EPI == EPI_HIST) hist_chunk(va, hw, ia.shift, ia.pmask, ia.pmask ? ia.pval[s.e] : 0);
+                            else emit_chunk(va, s.e, flat0 + 32 * h, ia.thr[s.e], ia, lane);
                         }
-                    } else if (j0 < j1) {
+                    } else if (j0 < j1 && EPI == EPI_DENSE_ABS) {
                         uint32_t va[32], vb[32];
                         tmem_ld_32x32b_x32(tb + 32 * j0, va);
                         tmem_ld_32x32b_x32(tb + 32 * j0 + 32, vb);
@@ -950,14 +937,12 @@ int sddmm_tc_dense_abs(const usaf_route_plan *pl, int R, int C, const __nv_bfloa
 // expert e with (key & pmask) == pval[e] (experts without slots are skipped)
 int sddmm_tc_key_hist(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
                       const __nv_bfloat16 *gin, int shift, int pmask, const int32_t *pval,
-                      unsigned int *hist, float *part, const int32_t *part_slot, cudaStream_t st) {
+                      unsigned int *hist, cudaStream_t st) {
     ImpArgs ia{};
     ia.shift = shift;
     ia.pmask = pmask;
     ia.pval = pval;
     ia.hist = hist;
-    ia.part = part;
-    ia.part_slot = part_slot;
     return sddmm_tc_launch<EPI_HIST>(pl, R, C, gout, gin, nullptr, nullptr, nullptr, st, ia);
 }
 
@@ -967,7 +952,7 @@ int sddmm_tc_key_hist(const usaf_route_plan *pl, int R, int C, const __nv_bfloat
 int sddmm_tc_key_emit(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
                       const __nv_bfloat16 *gin, const int32_t *thr, int64_t k, const int32_t *cand_row,
                       int32_t *n_gt, int32_t *n_eq, float *gt_val, int64_t *gt_idx, const int64_t *eq_off,
-                      float *eq_val, int64_t *eq_idx, float *part, const int32_t *part_slot, cudaStream_t st) {
+                      float *eq_val, int64_t *eq_idx, cudaStream_t st) {
     ImpArgs ia{};
     ia.thr = thr;
     ia.k = k;
@@ -979,8 +964,6 @@ int sddmm_tc_key_emit(const usaf_route_plan *pl, int R, int C, const __nv_bfloat
     ia.eq_off = eq_off;
     ia.eq_val = eq_val;
     ia.eq_idx = eq_idx;
-    ia.part = part;
-    ia.part_slot = part_slot;
     return sddmm_tc_launch<EPI_EMIT>(pl, R, C, gout, gin, nullptr, nullptr, nullptr, st, ia);
 }
 

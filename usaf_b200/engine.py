@@ -71,14 +71,6 @@ def expert_candidates(plan, expert_cnt: torch.Tensor, R: int, C: int, gout: torc
     cand_row = torch.full((E,), -1, dtype=torch.int32)
     cand_row[experts] = torch.arange(n_act, dtype=torch.int32)
     cand_row = cand_row.to(dev)
-    # fp32 partial sums of the experts whose slots span several SDDMM chunks
-    big = (cnt_h > int(_lib.LIB.usaf_importance_chunk_slots())).nonzero().reshape(-1)
-    part = part_slot = None
-    if big.numel():
-        ps = torch.full((E,), -1, dtype=torch.int32)
-        ps[big] = torch.arange(big.numel(), dtype=torch.int32)
-        part_slot = ps.to(dev)
-        part = torch.empty(big.numel() * R * C, dtype=torch.float32, device=dev)
     st = stream()
     hist = torch.zeros(E * 256, **i32)
     pval = torch.empty(E, **i32)
@@ -86,10 +78,10 @@ def expert_candidates(plan, expert_cnt: torch.Tensor, R: int, C: int, gout: torc
     thr = torch.empty(E, **i32)
     n_eq = torch.empty(E, **i64)
     args = (ptr(gout), ptr(gin), dtc)
-    call("usaf_importance_hist", plan, R, C, *args, 1, None, ptr(hist), ptr(part), ptr(part_slot), st)
+    call("usaf_importance_hist", plan, R, C, *args, 1, None, ptr(hist), st)
     call("usaf_importance_pick", ptr(hist), E, k, ptr(expert_cnt), 1, ptr(pval), ptr(need), None, None, st)
     hist.zero_()
-    call("usaf_importance_hist", plan, R, C, *args, 2, ptr(pval), ptr(hist), ptr(part), ptr(part_slot), st)
+    call("usaf_importance_hist", plan, R, C, *args, 2, ptr(pval), ptr(hist), st)
     call("usaf_importance_pick", ptr(hist), E, k, None, 2, ptr(pval), ptr(need), ptr(thr), ptr(n_eq), st)
     eq_off = torch.cumsum(n_eq, 0) - n_eq
     n_ties = int(n_eq.sum())                       # host read: sizes the tie lists
@@ -101,7 +93,7 @@ def expert_candidates(plan, expert_cnt: torch.Tensor, R: int, C: int, gout: torc
     n_gt = torch.zeros(E, **i32)
     n_eqc = torch.zeros(E, **i32)
     call("usaf_importance_emit", plan, R, C, *args, ptr(thr), k, ptr(cand_row), ptr(n_gt), ptr(n_eqc),
-         ptr(vals), ptr(idx), ptr(eq_off), ptr(eq_val), ptr(eq_idx), ptr(part), ptr(part_slot), st)
+         ptr(vals), ptr(idx), ptr(eq_off), ptr(eq_val), ptr(eq_idx), st)
     if n_ties:
         # ties at the threshold resolve to the lowest flat index: order the tie
         # lists by index and take each expert's first need[e]
