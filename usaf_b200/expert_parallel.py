@@ -159,7 +159,9 @@ class ExpertParallelMoE:
     def _own_buffers(self, rows: int):
         if rows <= self.cap:
             return
-        cap = max(rows, 1)
+        # grow with headroom: the routed rows drift up as the router trains, and every
+        # regrowth allocates seven buffers (an allocation stalls the stream)
+        cap = max(-(-int(rows * 1.25) // 256) * 256, 256)
         act = dict(dtype=self.dt, device=self.dev)
         H, I = self.H, self.I
         self.x_own = torch.empty(cap, H, **act)
