@@ -431,6 +431,30 @@ __device__ __forceinline__ void emit_chunk(const uint32_t (&v)[32], int e, int64
     }
 }
 
+// Tile order inside a run (one expert and column block, row blocks rb0..rb1,
+// the expert's slots in n chunks).  The sparse mode keeps a loaded chunk
+// resident across the run's row blocks (chunk outer, row block inner) and an
+// expert above one chunk sums its chunks through the compact output (only the
+// selected coordinates); the dense and importance modes keep every
+// coordinate, so they take row block outer, chunk inner, and sum the chunks
+// in the row block's TMEM accumulator (the chunks are reloaded per row block).
+struct TileOrder {
+    bool rb_outer, multi;
+    int rb0, rb1, n;
+    __device__ __forceinline__ int n_outer() const { return rb_outer ? rb1 - rb0 : n; }
+    __device__ __forceinline__ int n_inner() const { return rb_outer ? n : rb1 - rb0; }
+    __device__ __forceinline__ void at(int i, int j, int &rb, int &kc) const {
+        rb = rb0 + (rb_outer ? i : j);
+        kc = rb_outer ? j : i;
+    }
+    // the tile (rb, kc) loads its chunk / is the last to use it
+    __device__ __forceinline__ bool loads_b(int rb) const { return (rb_outer && multi) || rb == rb0; }
+    __device__ __forceinline__ bool frees_b(int rb) const { return (rb_outer && multi) || rb == rb1 - 1; }
+    // the tile starts / completes an accumulator
+    __device__ __forceinline__ bool acc_start(int kc) const { return !rb_outer || kc == 0; }
+    __device__ __forceinline__ bool acc_end(int kc) const { return !rb_outer || kc == n - 1; }
+};
+
 template <int EPI>
 __global__ void __launch_bounds__(kSThreads, 1)
     sddmm_tc_kernel(const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_in,
@@ -500,14 +524,13 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const int c0 = s.cb * kSN;
                 const int nb = min(4, (C - c0) / 64);
                 const bool ragged = ch.nk > 0 && ((cnt - (ch.nk - 1) * kSK) & 15) != 0;
-                // an expert within one chunk keeps its gin block resident for the whole run;
-                // a larger one reloads chunk after chunk for every row block, and the row
-                // block's accumulator sums all of them (no partial sums leave the SM)
-                const bool multi = ch.n > 1;
-                for (int rb = s.rb0; rb < s.rb1 && ok && ch.n; ++rb) {
-                    for (int kc = 0; kc < ch.n && ok; ++kc) {
+                const TileOrder to{EPI != EPI_SPARSE, ch.n > 1, s.rb0, s.rb1, ch.n};
+                for (int i = 0; i < to.n_outer() && ok && ch.n; ++i) {
+                    for (int j = 0; j < to.n_inner() && ok; ++j) {
+                        int rb, kc;
+                        to.at(i, j, rb, kc);
                         const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
-                        if (multi || rb == s.rb0) {
+                        if (to.loads_b(rb)) {
                             // the previous chunk's MMAs have read the resident block
                             if (!mbar_wait(&S.b_empty, (bc & 1) ^ 1, abort_flag, err)) {
                                 ok = false;
@@ -568,15 +591,19 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const int nb = min(4, (C - s.cb * kSN) / 64);
                 const uint32_t idesc = idesc_mn(kSM, nb * 64);
                 const bool ragged = ch.nk > 0 && ((cnt - (ch.nk - 1) * kSK) & 15) != 0;
-                const bool multi = ch.n > 1;
+                const TileOrder to{EPI != EPI_SPARSE, ch.n > 1, s.rb0, s.rb1, ch.n};
                 // (an expert without slots has no tiles: nothing to issue or drain)
-                for (int rb = s.rb0; rb < s.rb1 && ok && ch.n; ++rb, ++it) {
-                    const int buf = it & 1;
-                    if (!(ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err))) break;
-                    tc_fence_after();
-                    for (int kc = 0; kc < ch.n && ok; ++kc) {
+                for (int i = 0; i < to.n_outer() && ok && ch.n; ++i) {
+                    for (int j = 0; j < to.n_inner() && ok; ++j) {
+                        int rb, kc;
+                        to.at(i, j, rb, kc);
                         const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
-                        const bool new_b = multi || rb == s.rb0;
+                        const bool new_b = to.loads_b(rb);
+                        const int buf = it & 1;
+                        if (to.acc_start(kc)) {
+                            if (!(ok = mbar_wait(&S.acc_empty[buf], ((it >> 1) & 1) ^ 1, abort_flag, err))) break;
+                            tc_fence_after();
+                        }
                         for (int kb = kb0; kb < kb1; ++kb, ++ga) {
                             const int kbl = kb - kb0, st = ga % AST;
                             // first use of a loaded chunk: the resident block is in place
@@ -594,8 +621,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             const uint64_t da = dA0 + (uint64_t)((st * kAStage) >> 4);
                             const uint64_t db = dB0 + (uint64_t)((kbl * kBKb) >> 4);
                             const uint32_t dt = tbase + buf * kSN;
-                            // the row block's accumulator sums every chunk of the expert
-                            const bool first = kc == 0 && kb == kb0;
+                            // a row-block-outer accumulator sums every chunk of the expert
+                            const bool first = to.acc_start(kc) && kb == kb0;
                             if (kb < ch.nk - 1) {   // a full k-block: four MMAs
 #pragma unroll
                                 for (int kk = 0; kk < 4; ++kk)
@@ -608,15 +635,16 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             mma_commit(&S.a_empty[st]);
                         }
                         if (!ok) break;
-                        // the loaded chunk is done with: every chunk of a large expert, the
-                        // run's single chunk after its last row block
-                        if (multi || rb == s.rb1 - 1) {
+                        if (to.acc_end(kc)) {
+                            mma_commit(&S.acc_full[buf]);
+                            ++it;
+                        }
+                        // the loaded chunk is done with
+                        if (to.frees_b(rb)) {
                             mma_commit(&S.b_empty);
                             ++bc;
                         }
                     }
-                    if (!ok) break;
-                    mma_commit(&S.acc_full[buf]);
                 }
             }
             // every MMA this CTA issued has completed before TMEM is released
@@ -639,14 +667,16 @@ __global__ void __launch_bounds__(kSThreads, 1)
             // belongs to the next expert and is zeroed in both operands
             const int rem = cnt - (ch.nk - 1) * kSK;
             const bool ragged = ch.nk > 0 && (rem & 15) != 0;
-            const bool multi = ch.n > 1;
-            for (int rb = s.rb0; rb < s.rb1 && ok && ch.n; ++rb) {
-                for (int kc = 0; kc < ch.n && ok; ++kc) {
+            const TileOrder to{EPI != EPI_SPARSE, ch.n > 1, s.rb0, s.rb1, ch.n};
+            for (int i = 0; i < to.n_outer() && ok && ch.n; ++i) {
+                for (int j = 0; j < to.n_inner() && ok; ++j) {
+                    int rb, kc;
+                    to.at(i, j, rb, kc);
                     const int kb0 = kc * ch.per, kb1 = min(ch.nk, kb0 + ch.per);
                     for (int kb = kb0; kb < kb1; ++kb, ++ga) {
                         const int kbl = kb - kb0, st = ga % AST;
                         const bool tail = ragged && kb == ch.nk - 1;
-                        if (multi || rb == s.rb0) {
+                        if (to.loads_b(rb)) {
                             if (!(ok = warp_wait(&S.b_full[kbl], bc & 1, abort_flag, err))) break;
                             if (tail) {
                                 zero_tail(b_res + (size_t)kbl * kBKb, nb, rem, lane);
@@ -676,7 +706,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                             tail_par ^= 1u << st;
                         }
                     }
-                    if (multi || rb == s.rb1 - 1) ++bc;
+                    if (to.frees_b(rb)) ++bc;
                 }
             }
         }
@@ -728,16 +758,22 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 }
                 continue;
             }
-            {
-                // one drain per row block: its accumulator holds the sum over every chunk
-                const int mode = PART_ALL;
-                // this row's selection in the warp's two chunks and its first CSR
-                // positions in the two halves: loaded one row block ahead, so the
-                // loads' latency hides behind a whole tile
-                const bool sel = EPI == EPI_SPARSE && j0 < j1;
-                SliceRaw nxt = {};
-                if (sel) nxt = slice_load(mask, cbptr, (int64_t)s.e * R + s.rb0 * kSM + rr, C, ncb, s.cb, slice);
-                for (int rb = s.rb0; rb < s.rb1; ++rb, ++it) {
+            const TileOrder to{EPI != EPI_SPARSE, ch.n > 1, s.rb0, s.rb1, ch.n};
+            // this row's selection in the warp's two chunks and its first CSR positions
+            // in the two halves: loaded one row block ahead, so the loads' latency hides
+            // behind a whole tile (sparse mode: chunk outer, row block inner)
+            const bool sel = EPI == EPI_SPARSE && j0 < j1;
+            SliceRaw nxt = {};
+            for (int i = 0; i < to.n_outer() && ok; ++i) {
+                for (int jj = 0; jj < to.n_inner(); ++jj) {
+                    int rb, kc;
+                    to.at(i, jj, rb, kc);
+                    if (!to.acc_end(kc)) continue;          // the accumulator still sums chunks
+                    // a row-block-outer accumulator holds the sum over every chunk; the
+                    // sparse mode sums the chunks through the compact output
+                    const int mode = to.rb_outer || ch.n == 1 ? PART_ALL
+                                   : kc == 0 ? PART_FIRST : kc == ch.n - 1 ? PART_LAST : PART_MID;
+                    if (sel && jj == 0) nxt = slice_load(mask, cbptr, (int64_t)s.e * R + s.rb0 * kSM + rr, C, ncb, s.cb, slice);
                     const int64_t grow = (int64_t)s.e * R + rb * kSM + rr;   // global storage row
                     uint2 mw = make_uint2(0, 0);
                     int p0 = 0, p1 = 0;
@@ -784,6 +820,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                     }
                     tc_fence_before();
                     mbar_arrive(&S.acc_empty[buf]);
+                    ++it;
                 }
             }
             if (EPI == EPI_HIST) {
