@@ -124,6 +124,40 @@ def test_router_ties_fixture(dev, golden_dir):
     assert int((wt.cpu() != 0).sum(1).max()) > t["k"]
 
 
+@pytest.mark.parametrize("E,H", [(8, 6144), (16, 512), (128, 2048)])
+def test_router_logits_tensor_core_path(dev, E, H):
+    """usaf_router_fwd with a workspace takes the tcgen05 GEMM (split-K partials
+    summed in a fixed order, then one rounding to bf16); the logits agree with
+    an fp32 product rounded to bf16 to one bf16 ulp, and the routing mask with
+    the CUDA-core path (no workspace) wherever the two paths' logits agree."""
+    from usaf_b200 import _lib
+    torch.manual_seed(11)
+    T, k = 300, 2 if E == 8 else 4
+    x = torch.randn(T, H).to(torch.bfloat16)
+    w_r = (torch.randn(E, H) * 0.02).to(torch.bfloat16)
+    ref = (x.float() @ w_r.float().T).to(torch.bfloat16).float()
+    xd, wd = x.to(dev), w_r.to(dev)
+    ws = torch.empty(int(_lib.LIB.usaf_router_workspace_bytes(T, H, E)), dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    outs = []
+    for wsp in (_lib.ptr(ws), None):
+        lg = torch.empty(T, E, device=dev)
+        pr = torch.empty(T, E, device=dev)
+        wsum = torch.empty(T, device=dev)
+        wt = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
+        _lib.call("usaf_router_fwd", _lib.ptr(xd), _lib.ptr(wd), _lib.BF16, T, H, E, k, 1,
+                  _lib.ptr(lg), _lib.ptr(pr), _lib.ptr(wsum), _lib.ptr(wt), wsp,
+                  _lib.ptr(err) if wsp is not None else None, _lib.stream())
+        outs.append((lg.cpu(), wt.cpu()))
+    assert int(err.item()) == 0
+    (lg_tc, wt_tc), (lg_cc, wt_cc) = outs
+    for lg in (lg_tc, lg_cc):
+        assert ((lg - ref).abs() <= ref.abs() * 2 ** -7 + 1e-6).all()
+    same = (lg_tc == lg_cc).all(1)
+    assert same.float().mean() > 0.5
+    assert torch.equal((wt_tc != 0)[same], (wt_cc != 0)[same])
+
+
 # --------------------------------------------------------------- dispatch --
 def test_dispatch_matches_reference_indices(dev, golden_dir):
     from usaf_b200.engine import BlockDims, MoEBlock

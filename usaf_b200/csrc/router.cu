@@ -324,8 +324,10 @@ static RouterWs carve(void *ws, int T, int H, int E) {
     return w;
 }
 
+// E a multiple of 8: the [T][E] bf16 dlogits rows start on 16-byte boundaries
+// (TMA); tiles past E and H read as zero.
 static bool router_tc_ok(int T, int H, int E, const void *ws) {
-    return ws && dense_tc_available() && H % 64 == 0 && E % 64 == 0 && T >= 1;
+    return ws && dense_tc_available() && H % 64 == 0 && E % 8 == 0 && T >= 1;
 }
 
 }  // namespace usaf
@@ -400,12 +402,12 @@ extern "C" int usaf_router_bwd(const usaf_route_plan *plan, const void *x, const
         // dX_r [T][H] = dl [T][E] * W_r [E][H]   (K = E, W_r read MN-major), straight
         // into dx_acc when its rows hold whole 128-column tiles
         if (H % 128 == 0) {
-            rc = dense_tc_direct(w.dl_bf, T, E, E, wb, E, H, H, (int)Tp, (int)Hp, E, dx_acc, H, T,
-                                 plan->err, st, true);
+            rc = dense_tc_direct(w.dl_bf, T, E, E, wb, E, H, H, (int)Tp, (int)Hp, (int)rup(E, 64), dx_acc,
+                                 H, T, plan->err, st, true);
             if (rc) return rc;
         } else {
-            rc = dense_tc_partials(w.dl_bf, T, E, E, wb, E, H, H, (int)Tp, (int)Hp, E, 1, w.part, plan->err, st,
-                                   true);
+            rc = dense_tc_partials(w.dl_bf, T, E, E, wb, E, H, H, (int)Tp, (int)Hp, (int)rup(E, 64), 1, w.part,
+                                   plan->err, st, true);
             if (rc) return rc;
             finalize_partials<<<cdiv((int64_t)T * H, 256), 256, 0, st>>>(w.part, 1, (int)Tp, (int)Hp, T, H, 0,
                                                                          FIN_F32, dx_acc, H);
