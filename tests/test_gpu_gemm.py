@@ -96,6 +96,13 @@ CASES = [
     dict(T=16384, H=2048, E=128, k=8, I=768),
     # C5: Mixtral-8x22B-shaped experts (E=8, top-2, H=6144, I=16384)
     dict(T=256, H=6144, E=8, k=2, I=16384),
+    # decode-sized plans at the layer shapes: one token, 16 spread over the experts,
+    # 32 on a few experts, fully selected rows with few tokens, C5 experts
+    dict(T=1, H=2048, E=128, k=8, I=768),
+    dict(T=16, H=2048, E=128, k=8, I=768),
+    dict(T=32, H=2048, E=128, k=8, I=768, zipf=1.2),
+    dict(T=8, H=512, E=16, k=4, I=256, skew=True),
+    dict(T=4, H=6144, E=8, k=2, I=16384),
 ]
 
 
@@ -135,7 +142,7 @@ def test_grouped_gemms_vs_torch(dev, case):
     h_ref = (s * u).to(torch.bfloat16).float()
     check(blk.h[:P], h_ref, "swiglu")
     check(blk.y_seg[:P], y_ref, "down")
-    if "zipf" in case:
+    if "zipf" in case and case["T"] > 384:
         assert max(cnt) > 384
 
     # backward: dh = dcur @ W_dn[e] with SwiGLU backward fused; dx = dgu @ W_gu[e]
@@ -263,3 +270,4 @@ def test_in_kernel_dequant_bit_exact(dev, ci):
     assert torch.equal(blk.dx_seg[:P], want_bwd), \
         f"transposed: {int((blk.dx_seg[:P] != want_bwd).sum())} weights differ"
     assert off[-1] == P
+

@@ -101,6 +101,9 @@ CASES = [
     dict(T=320, H=512, E=16, k=2, I=256, zipf=0.0, seed=4, skew=False),    # experts of ~40 slots (< 64)
     dict(T=1024, H=2048, E=128, k=8, I=768, zipf=1.2, seed=5, skew=True),  # Qwen3-30B-A3B shapes
     dict(T=8, H=512, E=32, k=4, I=384, zipf=0.0, seed=6, skew=True),       # decode-sized: CUDA-core path
+    # experts of ~1000 slots on average: the streaming tensor-core kernel
+    dict(T=4096, H=512, E=8, k=2, I=384, zipf=0.0, seed=7, skew=True),
+    dict(T=4096, H=512, E=8, k=2, I=256, zipf=1.2, seed=8, skew=False),
 ]
 
 

@@ -24,9 +24,12 @@
 //   EPI_EMIT     : the same keys against a threshold per expert: every
 //                  coordinate above it goes to the expert's candidate list,
 //                  every one equal to it to the expert's tie list.
-//   An expert whose slots exceed one resident chunk is summed chunk after
-//   chunk into the same TMEM accumulator (its gin chunks reloaded for every
-//   row block), so no partial sums leave the SM in any mode.
+//   In the sparse mode an expert above one resident chunk (320 slots) is
+//   left to the streaming kernel of sddmm_stream.cu, launched after this one
+//   (it streams both operands and sums all of a tile's slots in one
+//   accumulator); the dense and importance modes sum such an expert chunk
+//   after chunk in the row block's TMEM accumulator (its gin chunks reloaded
+//   for every row block), so no partial sums leave the SM in any mode.
 //
 // Tile = 128 storage rows x 256 columns (MMA M x N), K = the expert's slots in
 // blocks of 64.  Both operands reach shared memory as TMA boxes of 64 slots x
@@ -43,9 +46,6 @@
 // (Expert-major numbering measured slower: each CTA then streams one
 // expert's gout once per column block, and 148 of those no longer fit in L2;
 // processing the experts in waves of 32 measured the same as this order.)
-// Experts with more slots run in chunks of at most 320 slots; the partial
-// sums of a chunk go through fp32 in the output vector and are rounded after
-// the last chunk.
 //
 // Warp 0 issues TMA; warp 18 zeroes the slots past an expert's end inside its
 // last 16-slot group (they belong to the next expert) and forwards those
@@ -57,6 +57,7 @@
 // so every scheduler has four drain warps to interleave.  TMEM holds two
 // 256-column accumulators, so the drain of one tile overlaps the MMAs of the
 // next.
+#include <climits>
 #include <cudaTypedefs.h>
 
 #include "tc_common.cuh"
@@ -81,8 +82,6 @@ constexpr uint32_t kFull = 0xffffffffu;
 
 enum : int { EPI_SPARSE = 0, EPI_DENSE_ABS = 1, EPI_HIST = 2, EPI_EMIT = 3 };
 constexpr int kHistBins = 256;
-// how a tile's sums combine with the other slot chunks of its expert
-enum : int { PART_ALL = 0, PART_FIRST = 1, PART_MID = 2, PART_LAST = 3 };
 
 struct alignas(8) SShared {
     uint64_t a_full[kAStages];
@@ -142,8 +141,10 @@ __device__ __forceinline__ float round_bf16(float v) {
 // ---- work order ----------------------------------------------------------------
 
 // cost of one tile of an expert with `cnt` slots, in units of one 16-slot MMA
-// step (the fixed part stands for the epilogue and the stream of gout)
-__device__ __forceinline__ int64_t tile_cost(int cnt, int dense) {
+// step (the fixed part stands for the epilogue and the stream of gout); an
+// expert above max_cnt slots is left to the streaming kernel (no cost here)
+__device__ __forceinline__ int64_t tile_cost(int cnt, int dense, int max_cnt) {
+    if (cnt > max_cnt) return 0;
     if (cnt <= 0) return dense == 2 ? 0 : dense ? 40 : 2;
     return (cnt + 15) / 16 + (dense ? 40 : 6);
 }
@@ -164,13 +165,13 @@ __device__ __forceinline__ int64_t warp_sum64(int64_t v) {
 
 // one warp: this CTA's tile range [t_lo, t_hi) -- the tiles whose cost prefix
 // falls in the CTA's equal share of the total
-__device__ void tile_range(const usaf_route_plan &pl, int nrb, int ncb, int dense, int lane, int *t_lo,
-                           int *t_hi) {
+__device__ void tile_range(const usaf_route_plan &pl, int nrb, int ncb, int dense, int max_cnt, int lane,
+                           int *t_lo, int *t_hi) {
     const int E = pl.E;
     int64_t We = 0;   // cost of one column block over all experts
     for (int e0 = 0; e0 < E; e0 += 32) {
         const int e = e0 + lane;
-        We += e < E ? tile_cost(__ldg(pl.expert_cnt + e), dense) * nrb : 0;
+        We += e < E ? tile_cost(__ldg(pl.expert_cnt + e), dense, max_cnt) * nrb : 0;
     }
     We = warp_sum64(We);
     const int64_t W = We * ncb, G = gridDim.x, b = blockIdx.x;
@@ -188,7 +189,7 @@ __device__ void tile_range(const usaf_route_plan &pl, int nrb, int ncb, int dens
         }
         for (int e0 = 0; e0 < E; e0 += 32) {
             const int e = e0 + lane;
-            const int64_t wt = e < E ? tile_cost(__ldg(pl.expert_cnt + e), dense) : 0;
+            const int64_t wt = e < E ? tile_cost(__ldg(pl.expert_cnt + e), dense, max_cnt) : 0;
             const int64_t w = wt * nrb;
             int64_t incl = w;
 #pragma unroll
@@ -206,8 +207,11 @@ __device__ void tile_range(const usaf_route_plan &pl, int nrb, int ncb, int dens
     }
     n0 = warp_sum64(n0);
     n1 = warp_sum64(n1);
+    // (the last CTA's bound W counts every tile of nonzero cost; trailing tiles
+    // of zero cost -- experts left to the streaming kernel, experts without
+    // slots in the histogram mode -- have no work and no CTA walks them)
     *t_lo = (int)n0;
-    *t_hi = b == G - 1 ? E * nrb * ncb : (int)n1;
+    *t_hi = (int)n1;
 }
 
 // a run of row blocks [rb0, rb1) of one (column block, expert) inside [t, t_hi)
@@ -266,26 +270,15 @@ __device__ __forceinline__ void st_na(float *p, float v) {
     asm volatile("st.global.L1::no_allocate.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
-__device__ __forceinline__ void emit_sparse(float *__restrict__ out, int mode, int p, float v) {
-    if (mode == PART_MID || mode == PART_LAST) v = __fadd_rn(out[p], v);
-    st_na(out + p, (mode == PART_ALL || mode == PART_LAST) ? round_bf16(v) : v);
-}
-
 // the selected columns of one 32-column chunk of this thread's row (values v,
 // bitmap word m), in ascending column order from CSR position p on: one
 // predicated store per column, straight-line code without a dependence from
 // one column to the next but the position counter
-__device__ __forceinline__ void drain_sparse(const uint32_t (&v)[32], uint32_t m, int &p, int mode,
+__device__ __forceinline__ void drain_sparse(const uint32_t (&v)[32], uint32_t m, int &p,
                                              float *__restrict__ out) {
-    if (mode == PART_ALL) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (m & (1u << i)) st_na(out + p++, round_bf16(__uint_as_float(v[i])));
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (m & (1u << i)) emit_sparse(out, mode, p++, __uint_as_float(v[i]));
-    }
+    for (int i = 0; i < 32; ++i)
+        if (m & (1u << i)) st_na(out + p++, round_bf16(__uint_as_float(v[i])));
 }
 
 // raw bitmap words and block start positions of one row's column block (the
@@ -337,21 +330,13 @@ __device__ __forceinline__ void slice_start(const uint32_t *__restrict__ mask, c
     p1 = pp.y + b1;
 }
 
-__device__ __forceinline__ void drain_dense(const uint32_t (&v)[32], float *o, int mode) {
+__device__ __forceinline__ void drain_dense(const uint32_t (&v)[32], float *o) {
     float4 *o4 = reinterpret_cast<float4 *>(o);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float4 a = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                               __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-        if (mode == PART_MID || mode == PART_LAST) {
-            const float4 b = o4[i];
-            a = make_float4(__fadd_rn(b.x, a.x), __fadd_rn(b.y, a.y), __fadd_rn(b.z, a.z), __fadd_rn(b.w, a.w));
-        }
-        if (mode == PART_ALL || mode == PART_LAST)
-            a = make_float4(fabsf(round_bf16(a.x)), fabsf(round_bf16(a.y)), fabsf(round_bf16(a.z)),
-                            fabsf(round_bf16(a.w)));
-        o4[i] = a;
-    }
+    for (int i = 0; i < 8; ++i)
+        o4[i] = make_float4(fabsf(round_bf16(__uint_as_float(v[4 * i]))), fabsf(round_bf16(__uint_as_float(v[4 * i + 1]))),
+                            fabsf(round_bf16(__uint_as_float(v[4 * i + 2]))),
+                            fabsf(round_bf16(__uint_as_float(v[4 * i + 3]))));
 }
 
 // ---- importance epilogues ---------------------------------------------------
@@ -432,12 +417,11 @@ __device__ __forceinline__ void emit_chunk(const uint32_t (&v)[32], int e, int64
 }
 
 // Tile order inside a run (one expert and column block, row blocks rb0..rb1,
-// the expert's slots in n chunks).  The sparse mode keeps a loaded chunk
-// resident across the run's row blocks (chunk outer, row block inner) and an
-// expert above one chunk sums its chunks through the compact output (only the
-// selected coordinates); the dense and importance modes keep every
-// coordinate, so they take row block outer, chunk inner, and sum the chunks
-// in the row block's TMEM accumulator (the chunks are reloaded per row block).
+// the expert's slots in n chunks).  The sparse mode only sees experts of one
+// chunk (larger ones go to the streaming kernel), kept resident across the
+// run's row blocks (chunk outer, row block inner); the dense and importance
+// modes take row block outer, chunk inner, and sum the chunks in the row
+// block's TMEM accumulator (the chunks are reloaded per row block).
 struct TileOrder {
     bool rb_outer, multi;
     int rb0, rb1, n;
@@ -459,7 +443,8 @@ template <int EPI>
 __global__ void __launch_bounds__(kSThreads, 1)
     sddmm_tc_kernel(const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_in,
                     usaf_route_plan pl, int R, int C, const uint32_t *__restrict__ mask,
-                    const int32_t *__restrict__ cbptr, float *__restrict__ out, const ImpArgs ia) {
+                    const int32_t *__restrict__ cbptr, float *__restrict__ out, const ImpArgs ia,
+                    int max_cnt) {
     // the histogram mode gives up one gout stage for the per-warp histograms
     constexpr int AST = EPI == EPI_HIST ? kAStages - 1 : kAStages;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -494,7 +479,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
             fence_barrier_init();
         }
         int lo, hi;
-        tile_range(pl, nrb, ncb, EPI == EPI_SPARSE ? 0 : EPI == EPI_DENSE_ABS ? 1 : 2, lane, &lo, &hi);
+        tile_range(pl, nrb, ncb, EPI == EPI_SPARSE ? 0 : EPI == EPI_DENSE_ABS ? 1 : 2, max_cnt, lane, &lo, &hi);
         if (lane == 0) {
             S.t_lo = lo;
             S.t_hi = hi;
@@ -519,6 +504,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const Run s = run_at(t, t_hi, nrb, pl.E);
                 t += s.rb1 - s.rb0;
                 const int cnt = pl.expert_cnt[s.e];
+                if (cnt > max_cnt) continue;   // the streaming kernel's expert
                 const int row0 = pl.expert_off[s.e];
                 const Chunks ch = chunks_of(cnt);
                 const int c0 = s.cb * kSN;
@@ -587,6 +573,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
                 const Run s = run_at(t, t_hi, nrb, pl.E);
                 t += s.rb1 - s.rb0;
                 const int cnt = pl.expert_cnt[s.e];
+                if (cnt > max_cnt) continue;
                 const Chunks ch = chunks_of(cnt);
                 const int nb = min(4, (C - s.cb * kSN) / 64);
                 const uint32_t idesc = idesc_mn(kSM, nb * 64);
@@ -661,6 +648,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
             const Run s = run_at(t, t_hi, nrb, pl.E);
             t += s.rb1 - s.rb0;
             const int cnt = pl.expert_cnt[s.e];
+            if (cnt > max_cnt) continue;
             const Chunks ch = chunks_of(cnt);
             const int nb = min(4, (C - s.cb * kSN) / 64);
             // slots of the expert's last k-block; the rest of its last 16-slot group
@@ -730,6 +718,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
             const Run s = run_at(t, t_hi, nrb, pl.E);
             t += s.rb1 - s.rb0;
             const int cnt = pl.expert_cnt[s.e];
+            if (cnt > max_cnt) continue;
             const Chunks ch = chunks_of(cnt);
             const int c0 = s.cb * kSN;
             // this warp's 32-column chunks of the block: [j0, j1)
@@ -769,10 +758,6 @@ __global__ void __launch_bounds__(kSThreads, 1)
                     int rb, kc;
                     to.at(i, jj, rb, kc);
                     if (!to.acc_end(kc)) continue;          // the accumulator still sums chunks
-                    // a row-block-outer accumulator holds the sum over every chunk; the
-                    // sparse mode sums the chunks through the compact output
-                    const int mode = to.rb_outer || ch.n == 1 ? PART_ALL
-                                   : kc == 0 ? PART_FIRST : kc == ch.n - 1 ? PART_LAST : PART_MID;
                     if (sel && jj == 0) nxt = slice_load(mask, cbptr, (int64_t)s.e * R + s.rb0 * kSM + rr, C, ncb, s.cb, slice);
                     const int64_t grow = (int64_t)s.e * R + rb * kSM + rr;   // global storage row
                     uint2 mw = make_uint2(0, 0);
@@ -792,10 +777,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         uint32_t va[32];
                         tmem_ld_32x32b_x32(tb + 32 * j0, va);
                         tmem_wait_ld();
-                        drain_sparse(va, mw.x, p0, mode, out);
+                        drain_sparse(va, mw.x, p0, out);
                         tmem_ld_32x32b_x32(tb + 32 * j0 + 32, va);
                         tmem_wait_ld();
-                        drain_sparse(va, mw.y, p1, mode, out);
+                        drain_sparse(va, mw.y, p1, out);
                     } else if (j0 < j1 && EPI >= EPI_HIST && !imp_skip) {
                         const int64_t lrow = (int64_t)rb * kSM + rr;   // row inside the expert
                         const int64_t flat0 = ((int64_t)s.e * R + lrow) * C + c0 + 32 * j0;
@@ -814,8 +799,8 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         tmem_wait_ld();
                         {
                             float *o = out + grow * C + c0 + 32 * j0;
-                            drain_dense(va, o, mode);
-                            drain_dense(vb, o + 32, mode);
+                            drain_dense(va, o);
+                            drain_dense(vb, o + 32);
                         }
                     }
                     tc_fence_before();
@@ -887,7 +872,7 @@ int s_num_sms() {
 template <int EPI>
 int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16 *gout,
                     const __nv_bfloat16 *gin, const uint32_t *mask, const int32_t *cbptr, float *out,
-                    cudaStream_t st, const ImpArgs &ia = ImpArgs{}) {
+                    cudaStream_t st, const ImpArgs &ia = ImpArgs{}, int max_cnt = INT_MAX) {
     CUtensorMap ta, tb;
     if (!s_tmap(&ta, gout, pl->P_cap, R) || !s_tmap(&tb, gin, pl->P_cap, C)) return USAF_EUNSUPPORTED;
     static bool attr = false;
@@ -900,7 +885,7 @@ int sddmm_tc_launch(const usaf_route_plan *pl, int R, int C, const __nv_bfloat16
     const int64_t tiles = (int64_t)pl->E * (R / kSM) * ((C + kSN - 1) / kSN);
     if (tiles == 0) return USAF_OK;
     dim3 grid((unsigned)std::min<int64_t>(s_num_sms(), tiles));
-    sddmm_tc_kernel<EPI><<<grid, kSThreads, kSSmem, st>>>(ta, tb, *pl, R, C, mask, cbptr, out, ia);
+    sddmm_tc_kernel<EPI><<<grid, kSThreads, kSSmem, st>>>(ta, tb, *pl, R, C, mask, cbptr, out, ia, max_cnt);
     USAF_CHECK_LAUNCH();
     return USAF_OK;
 }
@@ -946,12 +931,23 @@ __global__ void sddmm_accumulate_id(int n, const float *__restrict__ g, float sc
     }
 }
 
+int sddmm_stream_sparse(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *gout,
+                        const __nv_bfloat16 *gin, int min_cnt, float *scratch, cudaStream_t st);
+
 // g[j] (CSR order) = bf16(D[e][r][c]) for every overlay entry, then
 // compact[c2c[j]] += scale * g[j]
 int sddmm_tc_sparse(const usaf_route_plan *pl, const usaf_qweight *w, const __nv_bfloat16 *gout,
                     const __nv_bfloat16 *gin, const int32_t *c2c, float scale, float *compact,
                     float *scratch, cudaStream_t st) {
-    int rc = sddmm_tc_launch<EPI_SPARSE>(pl, w->R, w->C, gout, gin, w->ov_mask, w->ov_cbptr, scratch, st);
+    // experts of up to one resident chunk here; larger ones (only possible with
+    // more tokens than that, or an unknown token count) in the streaming kernel
+    // (sddmm_stream.cu), which sums a tile's slots in one accumulator instead of
+    // chunk by chunk
+    constexpr int kChunk = kBMaxKb * kSK;
+    int rc = sddmm_tc_launch<EPI_SPARSE>(pl, w->R, w->C, gout, gin, w->ov_mask, w->ov_cbptr, scratch, st,
+                                         ImpArgs{}, kChunk);
+    if (rc == USAF_OK && (pl->T <= 0 || pl->T > kChunk))
+        rc = sddmm_stream_sparse(pl, w, gout, gin, kChunk + 1, scratch, st);
     if (rc != USAF_OK) return rc;
     const int n = w->n_ov;
     if (!c2c && !((uintptr_t)scratch & 15) && !((uintptr_t)compact & 15)) {
