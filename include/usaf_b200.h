@@ -223,7 +223,11 @@ int usaf_expert_gate_up_bwd(const usaf_route_plan *plan, const usaf_qweight *w_g
  * [n_ov] per-coordinate partial sums.  bf16 with w->ov_mask runs on the
  * tensor cores unless the plan holds at most 64 pair slots per expert
  * (P_cap <= 64 * E, decode-sized batches), which take the CUDA-core kernel;
- * the results agree to bf16 rounding. */
+ * the results agree to bf16 rounding.  On the tensor cores an expert of up to
+ * 320 slots keeps its gin block resident across row blocks; when the plan
+ * may hold larger experts (plan->T > 320, or T == 0 for an unknown count) a
+ * second, streaming kernel takes those (plan->E <= 1024 then, else
+ * USAF_EUNSUPPORTED). */
 int usaf_sparse_dw(const usaf_route_plan *plan, const usaf_qweight *w, const void *gout,
                    const void *gin, int32_t dtype, const int32_t *csr_to_compact,
                    float scale, float *compact, float *scratch, void *stream);
