@@ -38,7 +38,7 @@ sys.path.insert(0, ROOT)
 
 CFG = dict(T=4096, H=2048, E=128, k=8, I=768, frac=0.005, lr=1e-4)
 # DRAM bytes (read + write) of one gate_up launch on this workload, from ncu
-GATE_UP_DRAM_BYTES = 372.6e6 + 129.3e6
+GATE_UP_DRAM_BYTES = 372.5e6 + 127.5e6
 
 
 def gate_up_bytes(n_pairs: int) -> float:
